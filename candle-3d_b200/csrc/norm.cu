@@ -1,0 +1,402 @@
+// Row-normalisation family: LayerNorm / RMSNorm fused with affine, adaLN
+// modulation, gates and residuals.  One kernel template covers
+//   l3d_layer_norm, l3d_layer_norm_modulate, l3d_gated_residual,
+//   l3d_layerscale_residual, l3d_residual_layer_norm_modulate,
+//   l3d_rms_norm_heads.
+//
+// Each row of C elements is owned by a group of G threads (G in 8..256); each
+// thread keeps up to NV 16-byte vectors of the row in registers, so the row is
+// read from HBM once and written once, with the reductions done by warp
+// shuffles (G <= 32) or shuffles plus one shared-memory exchange (G > 32).
+#include "common.cuh"
+
+namespace l3d {
+
+enum NormKind { NORM_NONE = 0, NORM_LAYER = 1, NORM_RMS = 2 };
+
+struct RowNormParams {
+  int64_t rows;
+  int64_t C;
+  int64_t rows_per_batch;  // row -> batch index for per-batch vectors
+  RowMap xm, hm, rm, ym;   // x, h (residual branch), r_out, y
+  const void* x;
+  const void* h;           // null: no residual branch
+  void* r_out;             // null: residual sum not stored
+  void* y;
+  ChanVec g1;              // gate on h (residual branch)
+  ChanVec w, b;            // affine
+  ChanVec scale, shift;    // adaLN modulation
+  ChanVec g2;              // gate on the normalised branch
+  int add_input;           // y += r after the gate
+  int norm;                // NormKind
+  float eps;
+};
+
+constexpr int kBlock = 256;
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v, float* red) {
+  if constexpr (G <= 32) {
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+  } else {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    constexpr int W = G / 32;  // warps per row group
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int grp = threadIdx.x / G;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < W; ++i) s += red[grp * W + i];
+    __syncthreads();
+    return s;
+  }
+}
+
+template <typename T, int VEC, int G, int kNV>
+__global__ void __launch_bounds__(kBlock) rownorm_kernel(const RowNormParams p) {
+  __shared__ float red[kBlock / 32];
+  constexpr int RPB = kBlock / G;  // rows per block
+  const int tid = threadIdx.x % G;
+  const int64_t row = int64_t(blockIdx.x) * RPB + threadIdx.x / G;
+  const bool valid = row < p.rows;
+  const int64_t nvec = p.C / VEC;
+  const int64_t b = valid ? row / p.rows_per_batch : 0;
+
+  const T* xr = static_cast<const T*>(p.x) + (valid ? row_offset(p.xm, row) : 0);
+  float v[kNV][VEC];
+#pragma unroll
+  for (int i = 0; i < kNV; ++i) {
+    const int64_t vi = tid + int64_t(i) * G;
+    if (valid && vi < nvec) load_act<T, VEC>(xr + vi * VEC, v[i]);
+    else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) v[i][e] = 0.f;
+    }
+  }
+  // Residual branch: r = x + g1 * h.
+  if (p.h) {
+    const T* hr = static_cast<const T*>(p.h) + (valid ? row_offset(p.hm, row) : 0);
+#pragma unroll
+    for (int i = 0; i < kNV; ++i) {
+      const int64_t vi = tid + int64_t(i) * G;
+      if (valid && vi < nvec) {
+        float hv[VEC];
+        load_act<T, VEC>(hr + vi * VEC, hv);
+        if (p.g1.ptr) {
+          float g[VEC];
+          load_chan<VEC>(p.g1, b, vi * VEC, g);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) hv[e] = hv[e] * g[e];
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[i][e] = v[i][e] + hv[e];
+      }
+    }
+    if (p.r_out) {
+      T* rr = static_cast<T*>(p.r_out) + (valid ? row_offset(p.rm, row) : 0);
+#pragma unroll
+      for (int i = 0; i < kNV; ++i) {
+        const int64_t vi = tid + int64_t(i) * G;
+        if (valid && vi < nvec) {
+          // Round the residual exactly as it is stored, so y is computed from
+          // the same values a later reader of r_out sees.
+          float t[VEC];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) t[e] = to_f(from_f<T>(v[i][e]));
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) v[i][e] = t[e];
+          store_act<T, VEC>(rr + vi * VEC, v[i]);
+        }
+      }
+    }
+  }
+
+  float inv = 1.f, mean = 0.f;
+  if (p.norm == NORM_LAYER) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNV; ++i)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) s += v[i][e];
+    s = group_sum<G>(s, red);
+    mean = s / float(p.C);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNV; ++i) {
+      const int64_t vi = tid + int64_t(i) * G;
+      if (vi < nvec) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float d = v[i][e] - mean;
+          ss += d * d;
+        }
+      }
+    }
+    ss = group_sum<G>(ss, red);
+    inv = 1.f / sqrtf(ss / float(p.C) + p.eps);
+  } else if (p.norm == NORM_RMS) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNV; ++i)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) ss += v[i][e] * v[i][e];
+    ss = group_sum<G>(ss, red);
+    inv = 1.f / sqrtf(ss / float(p.C) + p.eps);
+  }
+  if (!valid) return;
+
+  T* yr = static_cast<T*>(p.y) + row_offset(p.ym, row);
+#pragma unroll
+  for (int i = 0; i < kNV; ++i) {
+    const int64_t vi = tid + int64_t(i) * G;
+    if (vi >= nvec) continue;
+    const int64_t c0 = vi * VEC;
+    float o[VEC];
+    if (p.norm == NORM_NONE) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = v[i][e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = (v[i][e] - mean) * inv;
+      float t[VEC];
+      if (p.w.ptr) {
+        load_chan<VEC>(p.w, 0, c0, t);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = o[e] * t[e];
+      }
+      if (p.b.ptr) {
+        load_chan<VEC>(p.b, 0, c0, t);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = o[e] + t[e];
+      }
+      if (p.scale.ptr) {
+        load_chan<VEC>(p.scale, b, c0, t);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = o[e] * (1.f + t[e]);
+      }
+      if (p.shift.ptr) {
+        load_chan<VEC>(p.shift, b, c0, t);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = o[e] + t[e];
+      }
+      if (p.g2.ptr) {
+        load_chan<VEC>(p.g2, b, c0, t);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = t[e] * o[e];
+      }
+      if (p.add_input) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = o[e] + v[i][e];
+      }
+    }
+    store_act<T, VEC>(yr + c0, o);
+  }
+}
+
+template <typename T, int VEC, int NV>
+static void launch_rownorm_g(const RowNormParams& p, int G, cudaStream_t s) {
+  const int rpb = kBlock / G;
+  const int64_t blocks = (p.rows + rpb - 1) / rpb;
+  switch (G) {
+#define L3D_CASE(GG)                                                                      \
+  case GG: rownorm_kernel<T, VEC, GG, NV><<<dim3((unsigned)blocks), kBlock, 0, s>>>(p); break;
+    L3D_CASE(8) L3D_CASE(16) L3D_CASE(32) L3D_CASE(64) L3D_CASE(128) L3D_CASE(256)
+#undef L3D_CASE
+    default: break;
+  }
+}
+
+template <typename T, int VEC>
+static void launch_rownorm(const RowNormParams& p, int G, int NV, cudaStream_t s) {
+  if constexpr (VEC == 1) {
+    launch_rownorm_g<T, VEC, 16>(p, G, s);
+  } else {
+    if (NV <= 2) launch_rownorm_g<T, VEC, 2>(p, G, s);
+    else if (NV <= 4) launch_rownorm_g<T, VEC, 4>(p, G, s);
+    else launch_rownorm_g<T, VEC, 8>(p, G, s);
+  }
+}
+
+// Pick threads-per-row G and vectors-per-thread NV for a row of nvec vectors:
+// about four 16-byte vectors per thread keeps enough bytes in flight while
+// leaving registers for occupancy.
+static bool pick_geometry(int64_t nvec, bool scalar, int* G, int* NV) {
+  if (scalar) {  // ragged rows: up to 256 threads x 16 elements
+    int g = 8;
+    while (g < 256 && (nvec + g - 1) / g > 16) g *= 2;
+    *G = g;
+    *NV = 16;
+    return (nvec + g - 1) / g <= 16;
+  }
+  int g = 8;
+  while (g < 256 && g * 4 < nvec) g *= 2;
+  int64_t nv = (nvec + g - 1) / g;
+  int n = 2;
+  while (n < nv) n *= 2;
+  *G = g;
+  *NV = n;
+  return n <= 8;
+}
+
+struct RowNormArgs {
+  const l3d_tensor *x, *h, *g1, *w, *b, *scale, *shift, *g2, *r_out, *y;
+  int add_input;
+  int norm;
+  float eps;
+  const char* op;
+  int batch_dims;  // leading dims of x that form the batch of per-batch vectors (0 or 1)
+};
+
+static bool same_shape(const l3d_tensor* a, const l3d_tensor* b) {
+  if (a->ndim != b->ndim) return false;
+  for (int i = 0; i < a->ndim; ++i)
+    if (a->dims[i] != b->dims[i]) return false;
+  return true;
+}
+
+static int check_act(const l3d_tensor* t, const l3d_tensor* x, const char* op,
+                     const char* name) {
+  if (!t->data) return fail(L3D_E_NULL, "%s: %s has a null data pointer", op, name);
+  if (t->dtype != x->dtype)
+    return fail(L3D_E_DTYPE, "%s: %s dtype %s != x dtype %s", op, name, dtype_name(t->dtype),
+                dtype_name(x->dtype));
+  if (!same_shape(t, x)) return fail(L3D_E_SHAPE, "%s: %s shape differs from x", op, name);
+  if (t->dims[t->ndim - 1] > 1 && t->strides[t->ndim - 1] != 1)
+    return fail(L3D_E_ALIGN, "%s: %s last dim must be contiguous", op, name);
+  return L3D_OK;
+}
+
+static int run_rownorm(const RowNormArgs& a, cudaStream_t stream) {
+  const char* op = a.op;
+  if (!a.x || !a.y) return fail(L3D_E_NULL, "%s: x and y are required", op);
+  if (!a.x->data) return fail(L3D_E_NULL, "%s: x has a null data pointer", op);
+  if (!is_float_dtype(a.x->dtype)) return fail(L3D_E_DTYPE, "%s: x must be F32/F16/BF16", op);
+  if (a.x->ndim < 1 || a.x->ndim > L3D_MAX_DIMS) return fail(L3D_E_SHAPE, "%s: bad rank", op);
+  int rc;
+  if ((rc = check_act(a.y, a.x, op, "y"))) return rc;
+  if (a.h && (rc = check_act(a.h, a.x, op, "h"))) return rc;
+  if (a.r_out && (rc = check_act(a.r_out, a.x, op, "r_out"))) return rc;
+  if (a.x->dims[a.x->ndim - 1] > 1 && a.x->strides[a.x->ndim - 1] != 1)
+    return fail(L3D_E_ALIGN, "%s: x last dim must be contiguous", op);
+
+  RowNormParams p{};
+  p.C = a.x->dims[a.x->ndim - 1];
+  p.rows = 1;
+  for (int i = 0; i < a.x->ndim - 1; ++i) p.rows *= a.x->dims[i];
+  if (p.C <= 0) return fail(L3D_E_SHAPE, "%s: empty rows (C = 0)", op);
+  if (p.rows == 0) return L3D_OK;
+  int64_t B = 1;
+  if (a.batch_dims == 1 && a.x->ndim >= 3) B = a.x->dims[0];
+  p.rows_per_batch = p.rows / B;
+  const int lead = a.x->ndim - 1;
+  if (!make_rowmap(a.x, lead, &p.xm) || !make_rowmap(a.y, lead, &p.ym) ||
+      (a.h && !make_rowmap(a.h, lead, &p.hm)) || (a.r_out && !make_rowmap(a.r_out, lead, &p.rm)))
+    return fail(L3D_E_UNSUPPORTED, "%s: more than 5 non-collapsible leading dims", op);
+
+  bool al = true;
+  if ((rc = make_chanvec(a.g1, "gate", p.C, B, &p.g1, &al))) return rc;
+  if ((rc = make_chanvec(a.w, "weight", p.C, 1, &p.w, &al))) return rc;
+  if ((rc = make_chanvec(a.b, "bias", p.C, 1, &p.b, &al))) return rc;
+  if ((rc = make_chanvec(a.scale, "scale", p.C, B, &p.scale, &al))) return rc;
+  if ((rc = make_chanvec(a.shift, "shift", p.C, B, &p.shift, &al))) return rc;
+  if ((rc = make_chanvec(a.g2, "gate", p.C, B, &p.g2, &al))) return rc;
+  p.y = a.y->data;
+  p.h = a.h ? a.h->data : nullptr;
+  p.r_out = a.r_out ? a.r_out->data : nullptr;
+  p.x = a.x->data;
+  p.add_input = a.add_input;
+  p.norm = a.norm;
+  p.eps = a.eps;
+
+  const int es = dtype_size(a.x->dtype);
+  const int vec = 16 / es;
+  bool vec_ok = al && (p.C % vec == 0);
+  auto ptr_ok = [&](const l3d_tensor* t, const RowMap& m) {
+    return !t || ((reinterpret_cast<uintptr_t>(t->data) % 16) == 0 && rowmap_aligned(m, vec));
+  };
+  vec_ok = vec_ok && ptr_ok(a.x, p.xm) && ptr_ok(a.y, p.ym) && ptr_ok(a.h, p.hm) &&
+           ptr_ok(a.r_out, p.rm);
+  const int64_t vlen = vec_ok ? vec : 1;
+  const int64_t nvec = p.C / vlen;
+  int G = 8, NV = 8;
+  if (!pick_geometry(nvec, !vec_ok, &G, &NV))
+    return fail(L3D_E_UNSUPPORTED, "%s: row length %lld exceeds the per-row limit", op,
+                (long long)p.C);
+  L3D_DISPATCH_FLOAT(a.x->dtype, T, {
+    if (vec_ok) launch_rownorm<T, Vec16<T>::N>(p, G, NV, stream);
+    else launch_rownorm<T, 1>(p, G, NV, stream);
+  });
+  return check_launch(op);
+}
+
+}  // namespace l3d
+
+using namespace l3d;
+
+extern "C" int l3d_layer_norm(const l3d_tensor* x, const l3d_tensor* weight,
+                              const l3d_tensor* bias, float eps, const l3d_tensor* y,
+                              l3d_stream stream) {
+  RowNormArgs a{};
+  a.x = x; a.w = weight; a.b = bias; a.y = y; a.eps = eps;
+  a.norm = NORM_LAYER; a.op = "l3d_layer_norm"; a.batch_dims = 0;
+  return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int l3d_layer_norm_modulate(const l3d_tensor* x, const l3d_tensor* weight,
+                                       const l3d_tensor* bias, const l3d_tensor* shift,
+                                       const l3d_tensor* scale, const l3d_tensor* gate,
+                                       int add_input, float eps, const l3d_tensor* y,
+                                       l3d_stream stream) {
+  RowNormArgs a{};
+  a.x = x; a.w = weight; a.b = bias; a.shift = shift; a.scale = scale; a.g2 = gate;
+  a.add_input = add_input ? 1 : 0; a.y = y; a.eps = eps;
+  a.norm = NORM_LAYER; a.op = "l3d_layer_norm_modulate"; a.batch_dims = 1;
+  return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int l3d_gated_residual(const l3d_tensor* x, const l3d_tensor* h,
+                                  const l3d_tensor* gate, const l3d_tensor* out,
+                                  l3d_stream stream) {
+  if (!h || !gate) return fail(L3D_E_NULL, "l3d_gated_residual: h and gate are required");
+  RowNormArgs a{};
+  a.x = x; a.h = h; a.g1 = gate; a.y = out;
+  a.norm = NORM_NONE; a.op = "l3d_gated_residual"; a.batch_dims = 1;
+  return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int l3d_layerscale_residual(const l3d_tensor* x, const l3d_tensor* h,
+                                       const l3d_tensor* gamma, const l3d_tensor* out,
+                                       l3d_stream stream) {
+  if (!h || !gamma) return fail(L3D_E_NULL, "l3d_layerscale_residual: h and gamma are required");
+  if (gamma->ndim != 1)
+    return fail(L3D_E_SHAPE, "l3d_layerscale_residual: gamma must be [C]");
+  RowNormArgs a{};
+  a.x = x; a.h = h; a.g1 = gamma; a.y = out;
+  a.norm = NORM_NONE; a.op = "l3d_layerscale_residual"; a.batch_dims = 0;
+  return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int l3d_residual_layer_norm_modulate(
+    const l3d_tensor* x, const l3d_tensor* h, const l3d_tensor* gate, const l3d_tensor* weight,
+    const l3d_tensor* bias, const l3d_tensor* shift, const l3d_tensor* scale, float eps,
+    const l3d_tensor* r_out, const l3d_tensor* y, l3d_stream stream) {
+  if (!h) return fail(L3D_E_NULL, "l3d_residual_layer_norm_modulate: h is required");
+  RowNormArgs a{};
+  a.x = x; a.h = h; a.g1 = gate; a.w = weight; a.b = bias; a.shift = shift; a.scale = scale;
+  a.r_out = r_out; a.y = y; a.eps = eps;
+  a.norm = NORM_LAYER; a.op = "l3d_residual_layer_norm_modulate"; a.batch_dims = 1;
+  return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int l3d_rms_norm_heads(const l3d_tensor* x, const l3d_tensor* weight, float eps,
+                                  const l3d_tensor* y, l3d_stream stream) {
+  RowNormArgs a{};
+  a.x = x; a.w = weight; a.y = y; a.eps = eps;
+  a.norm = NORM_RMS; a.op = "l3d_rms_norm_heads"; a.batch_dims = 0;
+  return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
+}

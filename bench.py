@@ -40,13 +40,14 @@ METRIC = "layer-op HBM GB/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--rows", type=int, default=1 << 20, help="token rows per GPU")
     ap.add_argument("--channels", type=int, default=2048, choices=[1024, 1536, 2048])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
     return ap.parse_args()
 
@@ -73,7 +74,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                 "-i", str(self.idx), "-lms", "50"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -415,7 +416,7 @@ def main():
         del gathered
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle as orc
 
         orc.lib()

@@ -88,7 +88,7 @@ static int grid_for(int64_t work) {
 template <int A, bool GATED>
 static int run_act(const l3d_tensor* x, const l3d_tensor* y, const char* op,
                    cudaStream_t stream) {
-  if (!x || !y || !x->data || !y->data) return fail(L3D_E_NULL, "%s: x and y are required", op);
+  if (!x || !y || no_data(x) || no_data(y)) return fail(L3D_E_NULL, "%s: x and y are required", op);
   if (!is_float_dtype(x->dtype) || x->dtype != y->dtype)
     return fail(L3D_E_DTYPE, "%s: x/y must share a float dtype", op);
   if (x->ndim < 1 || x->ndim != y->ndim) return fail(L3D_E_SHAPE, "%s: rank mismatch", op);

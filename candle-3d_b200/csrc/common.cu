@@ -106,7 +106,7 @@ int make_chanvec(const l3d_tensor* t, const char* name, int64_t C, int64_t B, Ch
   out->bstride = 0;
   out->dtype = L3D_F32;
   if (!t) return L3D_OK;
-  if (!t->data) return fail(L3D_E_NULL, "%s: null data pointer", name);
+  if (no_data(t)) return fail(L3D_E_NULL, "%s: null data pointer", name);
   if (!is_float_dtype(t->dtype)) return fail(L3D_E_DTYPE, "%s: float dtype required", name);
   if (t->ndim < 1 || t->dims[t->ndim - 1] != C)
     return fail(L3D_E_SHAPE, "%s: last dim must be %lld", name, (long long)C);

@@ -44,6 +44,9 @@ inline int64_t numel(const l3d_tensor* t) {
   for (int i = 0; i < t->ndim; ++i) n *= t->dims[i];
   return n;
 }
+// A view that holds elements but no storage pointer (empty views may carry
+// a null pointer, as torch / Candle empty tensors do).
+inline bool no_data(const l3d_tensor* t) { return !t->data && numel(t) != 0; }
 
 // --------------------------------------------------------------- row mapping
 // Maps a flat row index over the leading dims of a view to an element offset.

@@ -237,7 +237,7 @@ using namespace l3d;
 extern "C" int l3d_timestep_embedding(const l3d_tensor* t, int dim, int order, float max_period,
                                       const l3d_tensor* out, l3d_stream stream) {
   const char* op = "l3d_timestep_embedding";
-  if (!t || !out || !t->data || !out->data) return fail(L3D_E_NULL, "%s: t and out required", op);
+  if (!t || !out || no_data(t) || no_data(out)) return fail(L3D_E_NULL, "%s: t and out required", op);
   if (t->dtype != L3D_F32) return fail(L3D_E_DTYPE, "%s: t must be F32", op);
   if (!is_float_dtype(out->dtype)) return fail(L3D_E_DTYPE, "%s: out must be a float dtype", op);
   if (order != 0 && order != 1) return fail(L3D_E_UNSUPPORTED, "%s: order must be 0 or 1", op);
@@ -269,7 +269,7 @@ extern "C" int l3d_linear_small(const l3d_tensor* x, const l3d_tensor* w, const 
                                 const l3d_tensor* addend, int act_in, int act_out,
                                 const l3d_tensor* y, l3d_stream stream) {
   const char* op = "l3d_linear_small";
-  if (!x || !w || !y || !x->data || !w->data || !y->data)
+  if (!x || !w || !y || no_data(x) || no_data(w) || no_data(y))
     return fail(L3D_E_NULL, "%s: x, w and y are required", op);
   if (!is_float_dtype(x->dtype) || !is_float_dtype(w->dtype) || !is_float_dtype(y->dtype))
     return fail(L3D_E_DTYPE, "%s: float dtypes required", op);
@@ -322,7 +322,7 @@ extern "C" int l3d_patch_embed(const l3d_tensor* pixels, const l3d_tensor* weigh
   const char* op = "l3d_patch_embed";
   const l3d_tensor* req[] = {pixels, weight, bias, pos, cls, out};
   for (const l3d_tensor* t : req)
-    if (!t || !t->data) return fail(L3D_E_NULL, "%s: pixels, weight, bias, pos, cls, out required", op);
+    if (!t || no_data(t)) return fail(L3D_E_NULL, "%s: pixels, weight, bias, pos, cls, out required", op);
   const int dt = pixels->dtype;
   if (dt != L3D_F32 && dt != L3D_BF16) return fail(L3D_E_DTYPE, "%s: F32 or BF16 required", op);
   for (const l3d_tensor* t : req)

@@ -1,18 +1,639 @@
-// Dequant-linear on the tensor cores (in progress).
+// Dequant-linear on the 5th-generation tensor cores (sm_100a).
+//
+//   y[M, N] = x[M, K] . deq(W)[N, K]^T (+ bias)   bf16 operands, f32 accumulate
+//
+// W arrives as raw GGML Q8_0 / Q4_0 blocks and is dequantised inside the
+// kernel, in the operand prologue, never materialised in HBM.  Persistent,
+// warp-specialised kernel, one CTA per SM, 128 x 256 output tiles, K in steps
+// of 64, a 3-stage shared-memory ring:
+//   warp 0       producer: one thread issues cp.async.bulk.tensor loads of the
+//                x tile (128 x 64 bf16, 128B swizzle) and of the raw block
+//                window of the W tile (256 rows x 96 B: the 16-byte-aligned
+//                window holding the two GGML blocks of this K step);
+//   warps 6..13  dequantisers: decode the raw window (f16 scale x int8 /
+//                nibble), round to bf16 and write the K-major 128B-swizzled B
+//                operand; fence.proxy.async, then arrive on the stage barrier;
+//   warp 1       MMA issuer: one thread issues tcgen05.mma kind::f16
+//                (M 128, N 256, K 16) into a double-buffered TMEM accumulator
+//                (2 x 256 f32 columns) and commits stage / tile barriers;
+//   warps 2..5   epilogue: tcgen05.ld of their TMEM lane quarter, + bias,
+//                convert, store; overlaps the next tile's MMA.
+// Weights whose rows are not 16-byte aligned (K % 256 != 0) are read by the
+// dequantisers straight from global memory instead of the TMA window.
+// Every mbarrier wait is bounded (wall-clock limit from %globaltimer); on
+// expiry the CTA records an error in the status word, stops issuing work and
+// still releases its TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "qlinear.cuh"
 
+namespace l3d {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+constexpr int RAW_ROW = 96;                 // bytes of the raw window per W row
+constexpr int A_BYTES = BM * BK * 2;        // 16 KB
+constexpr int B_BYTES = BN * BK * 2;        // 32 KB
+constexpr int RAW_BYTES = BN * RAW_ROW;     // 24 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + RAW_BYTES;
+constexpr int TMEM_COLS = 512;              // two 256-column accumulators
+constexpr int N_DQ_WARPS = 8;
+constexpr int THREADS = (6 + N_DQ_WARPS) * 32;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
+
+// Status word codes written by the kernel into the workspace header.
+constexpr int ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_TMEM = 3, ST_TIMEOUT_RAW = 4;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and raises the CTA abort flag) on timeout or
+// when another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// K-major, 128B-swizzled operand tile: rows of 128 B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3fffull;          // start address
+  d |= uint64_t(1) << 16;                // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;        // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;                // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;                // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M = 128, N = 256.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                           (uint32_t(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive f32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct Params {
+  int M, N, K;
+  const void* bias;   // [N] or null
+  int bias_dtype;
+  void* y;            // [M, N] rows of y_ld elements
+  int64_t y_ld;
+  int y_dtype;
+  int* status;        // workspace header
+  const uint8_t* wq;  // raw GGML blocks, rows of row_bytes
+  int64_t row_bytes;
+  int fmt;
+  int bpt;            // raw bytes per 64-wide K step (2 blocks)
+};
+
+// int8 -> f32 exactly: place (q ^ 0x80) = q + 128 in the mantissa of 2^23.
+__device__ __forceinline__ float i8_to_f(uint32_t byte) {
+  return __uint_as_float(0x4B000000u | (byte ^ 0x80u)) - 8388736.0f;
+}
+// 4-bit GGML code -> (code - 8) as f32.
+__device__ __forceinline__ float q4_to_f(uint32_t nib) {
+  return __uint_as_float(0x4B000000u | nib) - 8388616.0f;
+}
+
+// Decode one 32-weight block (2-byte aligned; src is smem or global) into
+// floats, w = d * q.
+template <bool GLOBAL>
+__device__ __forceinline__ void decode32(const uint8_t* blk, int fmt, float (&w)[32]) {
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(blk);
+  auto ld = [&](int i) -> uint32_t {
+    if constexpr (GLOBAL) return __ldg(h + i);
+    else return h[i];
+  };
+  const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(ld(0))));
+  if (fmt == L3D_Q8_0) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t v = ld(1 + j);
+      w[2 * j] = d * i8_to_f(v & 0xffu);
+      w[2 * j + 1] = d * i8_to_f(v >> 8);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t v = ld(1 + j);
+      w[2 * j] = d * q4_to_f(v & 15u);
+      w[2 * j + 1] = d * q4_to_f((v >> 8) & 15u);
+      w[16 + 2 * j] = d * q4_to_f((v >> 4) & 15u);
+      w[16 + 2 * j + 1] = d * q4_to_f(v >> 12);
+    }
+  }
+}
+
+// Dequantise the 256 x 64 W tile of (n0, kb) into the K-major SW128 layout:
+// row r occupies 128 B at (r / 8) * 1024 + (r % 8) * 128; its 16-byte chunk c
+// is stored at chunk (c ^ (r % 8)).  256 threads, 512 block jobs.
+template <bool RAW_TMA>
+__device__ __forceinline__ void dequant_tile(const Params& p, const uint8_t* raw, uint8_t* tile,
+                                             int n0, int kb, int t) {
+  const int bb = p.fmt == L3D_Q8_0 ? 34 : 18;
+  const int win_off = (kb * p.bpt) & 15;  // offset of the K step inside the 16-byte aligned window
+#pragma unroll 1
+  for (int job = t; job < BN * 2; job += N_DQ_WARPS * 32) {
+    const int r = job >> 1;      // tile row
+    const int half = job & 1;    // which 32-element block of the 64
+    const int n = n0 + r;
+    const int kblk = kb * 2 + half;
+    float w[32];
+    if (n < p.N && kblk * 32 < p.K) {
+      if constexpr (RAW_TMA) {
+        decode32<false>(raw + r * RAW_ROW + win_off + half * bb, p.fmt, w);
+      } else {
+        decode32<true>(p.wq + int64_t(n) * p.row_bytes + int64_t(kblk) * bb, p.fmt, w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) w[j] = 0.f;
+    }
+    uint8_t* row = tile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = w[c * 8 + e];
+      const int chunk = half * 4 + c;
+      *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) << 4)) = pack(f, __nv_bfloat16());
+    }
+  }
+}
+
+template <bool RAW_TMA>
+__global__ void __launch_bounds__(THREADS, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                 const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sa = smem;                              // [STAGES][A_BYTES]
+  uint8_t* sb = smem + STAGES * A_BYTES;           // [STAGES][B_BYTES]
+  uint8_t* sr = sb + STAGES * B_BYTES;             // [STAGES][RAW_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sr + STAGES * RAW_BYTES);
+  uint64_t* lfull = bars;                          // [STAGES] TMA -> dequant/MMA
+  uint64_t* bfull = bars + STAGES;                 // [STAGES] dequant -> MMA
+  uint64_t* empty = bars + 2 * STAGES;             // [STAGES] MMA -> producer
+  uint64_t* tfull = bars + 3 * STAGES;             // [2] MMA -> epilogue
+  uint64_t* tempty = bars + 3 * STAGES + 2;        // [2] epilogue -> MMA
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&lfull[s], 1);
+      mbar_init(&bfull[s], N_DQ_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
+          mbar_expect_tx(&lfull[stage], RAW_TMA ? A_BYTES + RAW_BYTES : A_BYTES);
+          tma_load_2d(sa + stage * A_BYTES, &map_x, &lfull[stage], kb * BK, m0);
+          if (RAW_TMA) {
+            // 16-byte aligned window (in 2-byte elements) holding this K step.
+            const int c0 = ((kb * p.bpt) >> 4) << 3;
+            tma_load_2d(sr + stage * RAW_BYTES, &map_w, &lfull[stage], c0, n0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, ST_TIMEOUT_TMEM)) break;
+        tc_fence_after();
+        const uint32_t dtm = tmem_base + uint32_t(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW) ||
+              !mbar_wait(&bfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(sa + stage * A_BYTES);
+          const uint64_t db = smem_desc_sw128(sb + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 B per K step inside the 128 B swizzle atom (encoded >> 4).
+            umma_bf16(dtm, da + uint64_t(2 * k), db + uint64_t(2 * k), (kb | k) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++local) {
+      const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, ST_TIMEOUT_TMEM)) break;
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(taddr + uint32_t(c), v);
+        const int col0 = n0 + c;
+        if (row < p.M && col0 < p.N) {
+          if (p.bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = col0 + i;
+              if (col < p.N)
+                v[i] += p.bias_dtype == L3D_F32
+                            ? __ldg(static_cast<const float*>(p.bias) + col)
+                            : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[col]);
+            }
+          }
+          if (p.y_dtype == L3D_BF16) {
+            __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + int64_t(row) * p.y_ld + col0;
+            if (col0 + 32 <= p.N) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = v[q * 8 + e];
+                *reinterpret_cast<uint4*>(yr + q * 8) = pack(f, __nv_bfloat16());
+              }
+            } else {
+              for (int i = 0; i < 32 && col0 + i < p.N; ++i) yr[i] = __float2bfloat16_rn(v[i]);
+            }
+          } else {
+            float* yr = static_cast<float*>(p.y) + int64_t(row) * p.y_ld + col0;
+            if (col0 + 32 <= p.N) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                *reinterpret_cast<float4*>(yr + q * 4) =
+                    make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+            } else {
+              for (int i = 0; i < 32 && col0 + i < p.N; ++i) yr[i] = v[i];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  } else {
+    // --------------------------------------------------------- dequantisers
+    const int t = threadIdx.x - 6 * 32;  // 0 .. 255
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      const int n0 = (tile % num_n) * BN;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        // The raw window (and the x tile) of this stage have landed, which also
+        // means the MMA has released the stage's B buffer.
+        if (!mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW)) {
+          ok = false;
+          break;
+        }
+        dequant_tile<RAW_TMA>(p, sr + stage * RAW_BYTES, sb + stage * B_BYTES, n0, kb, t);
+        // Generic-proxy smem writes must be visible to the tensor core.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+    }
+  }
+
+  // Teardown: every role has left its loop (normally or on abort).
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 32) {
+    // Drain before releasing TMEM and shared memory: wait (bounded) for every
+    // MMA this thread issued, then for every TMA load still in flight.
+    uint64_t* drain = bars + 3 * STAGES + 6;
+    mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    umma_commit(drain);
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < WAIT_LIMIT_NS) {
+    }
+    // TMA loads land within microseconds; give any still in flight 1 ms.
+    const uint64_t t1 = globaltimer();
+    while (globaltimer() - t1 < 1000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------- host
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// x: bf16 [rows, cols] with row stride ld elements; box rows x 64, 128B swizzle.
+static bool make_map_x(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                       uint64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {uint32_t(BK), uint32_t(BM)};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Raw blocks viewed as uint16 [n, row_bytes / 2]; box 256 rows x 48 elements (96 B).
+static bool make_map_w(CUtensorMap* m, const void* base, uint64_t n, uint64_t row_bytes) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {row_bytes / 2, n};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {uint32_t(RAW_ROW / 2), uint32_t(BN)};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace gemm
+
+// Convert f32 activations to bf16 (rows of ld elements -> contiguous [M, K]).
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, int64_t ld, int64_t M, int64_t K,
+                                   __nv_bfloat16* __restrict__ out) {
+  const int64_t total = M * K;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / K, c = i - r * K;
+    out[i] = __float2bfloat16_rn(x[r * ld + c]);
+  }
+}
+
+}  // namespace l3d
+
 using namespace l3d;
 
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace: [0, 256) status word; then a bf16 copy of the activations when x
+// is F32 or its rows are not 16-byte aligned.
 extern "C" size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t n, int64_t k) {
-  (void)fmt; (void)m;
-  return size_t(n) * size_t(k) * 2 + 256;
+  (void)fmt;
+  (void)n;
+  if (m < 0 || k < 0) return 0;
+  return 256 + align256(size_t(m) * size_t(k) * 2);
 }
 
 extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n,
                                   int64_t k, const l3d_tensor* bias, const l3d_tensor* y,
                                   void* workspace, size_t workspace_bytes, l3d_stream stream) {
-  (void)x; (void)wq; (void)fmt; (void)n; (void)k; (void)bias; (void)y; (void)workspace;
-  (void)workspace_bytes; (void)stream;
-  return fail(L3D_E_UNSUPPORTED, "l3d_dequant_linear: not built yet");
+  const char* op = "l3d_dequant_linear";
+  using namespace l3d::gemm;
+  if (!x || !y || !wq || no_data(x) || no_data(y))
+    return fail(L3D_E_NULL, "%s: x, wq and y are required", op);
+  if (fmt != L3D_Q8_0 && fmt != L3D_Q4_0) return fail(L3D_E_UNSUPPORTED, "%s: unknown format", op);
+  if (x->dtype != L3D_BF16 && x->dtype != L3D_F32)
+    return fail(L3D_E_DTYPE, "%s: x must be BF16 or F32", op);
+  if (y->dtype != L3D_BF16 && y->dtype != L3D_F32)
+    return fail(L3D_E_DTYPE, "%s: y must be BF16 or F32", op);
+  if (k <= 0 || k % 32 || n <= 0) return fail(L3D_E_SHAPE, "%s: k must be a positive multiple of 32", op);
+  if (x->ndim < 1 || x->dims[x->ndim - 1] != k) return fail(L3D_E_SHAPE, "%s: x last dim != k", op);
+  if (y->ndim != x->ndim || y->dims[y->ndim - 1] != n) return fail(L3D_E_SHAPE, "%s: y last dim != n", op);
+  int64_t M = 1;
+  for (int i = 0; i < x->ndim - 1; ++i) {
+    if (x->dims[i] != y->dims[i]) return fail(L3D_E_SHAPE, "%s: x/y leading dims differ", op);
+    M *= x->dims[i];
+  }
+  if (M > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+    return fail(L3D_E_UNSUPPORTED, "%s: dimensions exceed 2^31", op);
+  RowMap xm, ym;
+  if (!make_rowmap(x, x->ndim - 1, &xm) || !make_rowmap(y, y->ndim - 1, &ym) || xm.nd != 1 ||
+      ym.nd != 1)
+    return fail(L3D_E_ALIGN, "%s: x and y must be row-major matrices (one row stride)", op);
+  if ((k > 1 && x->strides[x->ndim - 1] != 1) || (n > 1 && y->strides[y->ndim - 1] != 1))
+    return fail(L3D_E_ALIGN, "%s: last dims must be contiguous", op);
+  const int64_t x_ld = M > 1 ? xm.strides[0] : k;
+  const int64_t y_ld = M > 1 ? ym.strides[0] : n;
+  if (bias) {
+    if (no_data(bias)) return fail(L3D_E_NULL, "%s: bias has no data", op);
+    if (bias->dtype != L3D_F32 && bias->dtype != L3D_BF16)
+      return fail(L3D_E_DTYPE, "%s: bias must be F32 or BF16", op);
+    if (numel(bias) != n || (bias->ndim >= 1 && n > 1 && bias->strides[bias->ndim - 1] != 1))
+      return fail(L3D_E_SHAPE, "%s: bias must be contiguous [n]", op);
+  }
+  if (reinterpret_cast<uintptr_t>(wq) % 2) return fail(L3D_E_ALIGN, "%s: wq must be 2-byte aligned", op);
+  const size_t need = l3d_dequant_linear_workspace_size(fmt, M, n, k);
+  if (!workspace || workspace_bytes < need)
+    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(L3D_E_ALIGN, "%s: workspace must be 256-byte aligned", op);
+  if (M == 0) return L3D_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  if (cudaMemsetAsync(status, 0, 256, s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: status clear failed", op);
+
+  // Activations as a bf16 [M, K] matrix with a 16-byte-aligned row stride.
+  const void* xa = elem_ptr(x);
+  int64_t lda = x_ld;
+  if (x->dtype == L3D_F32 || (lda * 2) % 16 || reinterpret_cast<uintptr_t>(xa) % 16) {
+    __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+    if (x->dtype == L3D_F32) {
+      int64_t blocks = (M * k + 255) / 256;
+      if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
+      f32_to_bf16_kernel<<<int(blocks), 256, 0, s>>>(static_cast<const float*>(xa), x_ld, M, k, xb);
+    } else {
+      if (cudaMemcpy2DAsync(xb, size_t(k) * 2, xa, size_t(x_ld) * 2, size_t(k) * 2, size_t(M),
+                            cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return fail(L3D_E_CUDA, "%s: activation copy failed", op);
+    }
+    xa = xb;
+    lda = k;
+  }
+  Params p{};
+  p.M = int(M); p.N = int(n); p.K = int(k);
+  p.bias = bias ? elem_ptr(bias) : nullptr;
+  p.bias_dtype = bias ? bias->dtype : L3D_F32;
+  p.y = const_cast<char*>(elem_ptr(y));
+  p.y_ld = y_ld;
+  p.y_dtype = y->dtype;
+  p.status = status;
+  p.wq = static_cast<const uint8_t*>(wq);
+  p.fmt = fmt;
+  p.row_bytes = (k / 32) * block_bytes(fmt);
+  p.bpt = 2 * block_bytes(fmt);
+  CUtensorMap map_x, map_w;
+  if (!make_map_x(&map_x, xa, uint64_t(M), uint64_t(k), uint64_t(lda)))
+    return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for x", op);
+  // The TMA window needs 16-byte aligned weight rows (k % 256 == 0).
+  const bool raw_tma = (reinterpret_cast<uintptr_t>(wq) % 16 == 0) && (p.row_bytes % 16 == 0) &&
+                       make_map_w(&map_w, wq, uint64_t(n), uint64_t(p.row_bytes));
+  if (!raw_tma) map_w = map_x;  // unused
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(qgemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(qgemm_kernel<false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: cannot reserve %d bytes of shared memory", op, SMEM_BYTES);
+  const int tiles = int(((M + BM - 1) / BM) * ((n + BN - 1) / BN));
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  if (raw_tma) qgemm_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(map_x, map_w, p);
+  else qgemm_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(map_x, map_w, p);
+  return check_launch(op);
 }

@@ -223,8 +223,8 @@ static void launch_rownorm(const RowNormParams& p, int G, int NV, cudaStream_t s
 }
 
 // Pick threads-per-row G and vectors-per-thread NV for a row of nvec vectors:
-// about four 16-byte vectors per thread keeps enough bytes in flight while
-// leaving registers for occupancy.
+// the smallest group that holds the row in at most eight 16-byte vectors per
+// thread, so each thread has all its loads in flight at once.
 static bool pick_geometry(int64_t nvec, bool scalar, int* G, int* NV) {
   if (scalar) {  // ragged rows: up to 256 threads x 16 elements
     int g = 8;
@@ -233,8 +233,10 @@ static bool pick_geometry(int64_t nvec, bool scalar, int* G, int* NV) {
     *NV = 16;
     return (nvec + g - 1) / g <= 16;
   }
+  // Up to eight 16-byte vectors per thread: a whole 2048-element bf16 (or
+  // 1024-element f32) row per warp, reduced with shuffles only.
   int g = 8;
-  while (g < 256 && g * 4 < nvec) g *= 2;
+  while (g < 256 && g * 8 < nvec) g *= 2;
   int64_t nv = (nvec + g - 1) / g;
   int n = 2;
   while (n < nv) n *= 2;
@@ -261,7 +263,7 @@ static bool same_shape(const l3d_tensor* a, const l3d_tensor* b) {
 
 static int check_act(const l3d_tensor* t, const l3d_tensor* x, const char* op,
                      const char* name) {
-  if (!t->data) return fail(L3D_E_NULL, "%s: %s has a null data pointer", op, name);
+  if (no_data(t)) return fail(L3D_E_NULL, "%s: %s has a null data pointer", op, name);
   if (t->dtype != x->dtype)
     return fail(L3D_E_DTYPE, "%s: %s dtype %s != x dtype %s", op, name, dtype_name(t->dtype),
                 dtype_name(x->dtype));
@@ -274,7 +276,7 @@ static int check_act(const l3d_tensor* t, const l3d_tensor* x, const char* op,
 static int run_rownorm(const RowNormArgs& a, cudaStream_t stream) {
   const char* op = a.op;
   if (!a.x || !a.y) return fail(L3D_E_NULL, "%s: x and y are required", op);
-  if (!a.x->data) return fail(L3D_E_NULL, "%s: x has a null data pointer", op);
+  if (no_data(a.x)) return fail(L3D_E_NULL, "%s: x has a null data pointer", op);
   if (!is_float_dtype(a.x->dtype)) return fail(L3D_E_DTYPE, "%s: x must be F32/F16/BF16", op);
   if (a.x->ndim < 1 || a.x->ndim > L3D_MAX_DIMS) return fail(L3D_E_SHAPE, "%s: bad rank", op);
   int rc;

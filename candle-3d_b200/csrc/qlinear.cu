@@ -68,7 +68,7 @@ using namespace l3d;
 extern "C" int l3d_dequantize(const void* wq, int fmt, int64_t n, int64_t k,
                               const l3d_tensor* out, l3d_stream stream) {
   const char* op = "l3d_dequantize";
-  if (!wq || !out || !out->data) return fail(L3D_E_NULL, "%s: wq and out are required", op);
+  if (!wq || !out || no_data(out)) return fail(L3D_E_NULL, "%s: wq and out are required", op);
   if (fmt != L3D_Q8_0 && fmt != L3D_Q4_0) return fail(L3D_E_UNSUPPORTED, "%s: unknown format", op);
   if (n < 0 || k < 0 || k % 32) return fail(L3D_E_SHAPE, "%s: k must be a multiple of 32", op);
   if (!is_float_dtype(out->dtype)) return fail(L3D_E_DTYPE, "%s: out must be a float dtype", op);

@@ -139,18 +139,29 @@ __global__ void __launch_bounds__(256) rope2d_kernel(const Rope2dParams p) {
       if (t >= p.ntensor) break;
       const HeadView& iv = p.in[t];
       const HeadView& ov = p.out[t];
-      for (int h0 = 0; h0 < p.H; h0 += 4) {
-        const int h = h0 + hg;
-        const bool valid = h < p.H;
-        float y[8];
-        if (valid) {
+      // Heads in groups of 4 iterations x 4 heads: the group's loads are all
+      // issued before any arithmetic.
+      constexpr int MAXIT = 4;
+      for (int hb = 0; hb < p.H; hb += 4 * MAXIT) {
+      float yy[MAXIT][8];
+#pragma unroll
+      for (int it = 0; it < MAXIT; ++it) {
+        const int h = hb + it * 4 + hg;
+        if (h < p.H) {
           const T* src = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + h * iv.sh +
                          n * iv.sn + 8 * m;
-          load8<T>(src, y);
+          load8<T>(src, yy[it]);
         } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = 0.f;
+          for (int i = 0; i < 8; ++i) yy[it][i] = 0.f;
         }
+      }
+#pragma unroll
+      for (int it = 0; it < MAXIT; ++it) {
+        if (hb + it * 4 >= p.H) break;  // warp-uniform
+        const int h = hb + it * 4 + hg;
+        const bool valid = h < p.H;
+        float* y = yy[it];
         if (p.do_norm) {
           float sum = 0.f;
 #pragma unroll
@@ -182,6 +193,7 @@ __global__ void __launch_bounds__(256) rope2d_kernel(const Rope2dParams p) {
           T* dst = static_cast<T*>(ov.data) + ov.base + b * ov.sb + h * ov.sh + n * ov.sn + 8 * m;
           store8<T>(dst, o);
         }
+      }
       }
     }
   }
@@ -287,19 +299,30 @@ __global__ void __launch_bounds__(256) rope3d_kernel(const Rope3dParams p) {
         }
       }
     }
-    for (int h0 = 0; h0 < p.H; h0 += HPI) {
-      const int h = h0 + hg;
-      const bool valid = h < p.H && lane_on;
-      float v[EPL];
+    // Heads in groups of MAXIT warp iterations: all loads of a group are issued
+    // before any arithmetic, so a warp keeps up to MAXIT x 512 B in flight.
+    constexpr int MAXIT = 8;
+    for (int hb = 0; hb < p.H; hb += HPI * MAXIT) {
+    float vv[MAXIT][EPL];
+#pragma unroll
+    for (int it = 0; it < MAXIT; ++it) {
+      const int h = hb + it * HPI + hg;
       const T* src = static_cast<const T*>(p.x) + p.xbase + b * p.xsb + l * p.xsl +
                      int64_t(h) * p.xsh + m * EPL;
-      if (valid) {
-        if constexpr (EPL == 8) load8<T>(src, v);
-        else { v[0] = to_f(src[0]); v[1] = to_f(src[1]); }
+      if (h < p.H && lane_on) {
+        if constexpr (EPL == 8) load8<T>(src, vv[it]);
+        else { vv[it][0] = to_f(src[0]); vv[it][1] = to_f(src[1]); }
       } else {
 #pragma unroll
-        for (int i = 0; i < EPL; ++i) v[i] = 0.f;
+        for (int i = 0; i < EPL; ++i) vv[it][i] = 0.f;
       }
+    }
+#pragma unroll
+    for (int it = 0; it < MAXIT; ++it) {
+      if (hb + it * HPI >= p.H) break;  // warp-uniform
+      const int h = hb + it * HPI + hg;
+      const bool valid = h < p.H && lane_on;
+      float* v = vv[it];
       if (p.gamma) {
         float ss = 0.f;
 #pragma unroll
@@ -328,6 +351,7 @@ __global__ void __launch_bounds__(256) rope3d_kernel(const Rope3dParams p) {
         else { dst[0] = from_f<T>(o[0]); dst[1] = from_f<T>(o[1]); }
       }
     }
+    }
   }
 }
 
@@ -354,7 +378,7 @@ __global__ void rope3d_tables_kernel(int64_t L, const void* coords, int cdt, int
 // ================================================================== host side
 static int head_view(const l3d_tensor* t, const char* op, const char* name, int64_t D,
                      HeadView* v) {
-  if (!t || !t->data) return fail(L3D_E_NULL, "%s: %s is required", op, name);
+  if (!t || no_data(t)) return fail(L3D_E_NULL, "%s: %s is required", op, name);
   if (t->ndim != 4) return fail(L3D_E_SHAPE, "%s: %s must be rank 4", op, name);
   if (t->dims[3] != D) return fail(L3D_E_SHAPE, "%s: %s last dim must be %lld", op, name,
                                    (long long)D);
@@ -419,7 +443,7 @@ static int run_rope2d(const l3d_tensor* const* xs, const l3d_tensor* const* ws,
   if (p.H > 4096) return fail(L3D_E_UNSUPPORTED, "%s: too many heads", op);
   if (p.B * p.N == 0 || p.H == 0) return L3D_OK;
   if (positions) {
-    if (!positions->data) return fail(L3D_E_NULL, "%s: positions has no data", op);
+    if (no_data(positions)) return fail(L3D_E_NULL, "%s: positions has no data", op);
     if (!is_index_dtype(positions->dtype))
       return fail(L3D_E_DTYPE, "%s: positions must be I32/I64/U32", op);
     if (positions->ndim != 3 || positions->dims[0] != p.B || positions->dims[1] != p.N ||
@@ -440,7 +464,7 @@ static int run_rope2d(const l3d_tensor* const* xs, const l3d_tensor* const* ws,
     int64_t* sns[2] = {&p.csn, &p.ssn};
     for (int i = 0; i < 2; ++i) {
       const l3d_tensor* tb = tabs[i];
-      if (!tb || !tb->data) return fail(L3D_E_NULL, "%s: cos/sin tables are required", op);
+      if (!tb || no_data(tb)) return fail(L3D_E_NULL, "%s: cos/sin tables are required", op);
       if (tb->dtype != L3D_F32) return fail(L3D_E_DTYPE, "%s: rope tables must be F32", op);
       // Accept [B, 1, N, 64] or [B, N, 64].
       int64_t tb_b, tb_n, tb_d, s_b, s_n, s_d;
@@ -511,8 +535,8 @@ extern "C" int l3d_rope2d_tables(const l3d_tensor* positions, float theta, int h
                                  const l3d_tensor* cos_full, const l3d_tensor* sin_alt_full,
                                  l3d_stream stream) {
   const char* op = "l3d_rope2d_tables";
-  if (!positions || !cos_full || !sin_alt_full || !positions->data || !cos_full->data ||
-      !sin_alt_full->data)
+  if (!positions || !cos_full || !sin_alt_full || no_data(positions) || no_data(cos_full) ||
+      no_data(sin_alt_full))
     return fail(L3D_E_NULL, "%s: positions, cos_full and sin_alt_full are required", op);
   if (head_dim <= 0 || head_dim % 4) return fail(L3D_E_SHAPE, "%s: head_dim must be a multiple of 4", op);
   if (!is_index_dtype(positions->dtype)) return fail(L3D_E_DTYPE, "%s: positions must be integer", op);
@@ -546,7 +570,7 @@ extern "C" int l3d_rope2d_tables(const l3d_tensor* positions, float theta, int h
 static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_tensor* coords,
                       float theta, const l3d_tensor* cos_t, const l3d_tensor* sin_t,
                       const l3d_tensor* y, const char* op, cudaStream_t stream) {
-  if (!x || !y || !x->data || !y->data) return fail(L3D_E_NULL, "%s: x and y are required", op);
+  if (!x || !y || no_data(x) || no_data(y)) return fail(L3D_E_NULL, "%s: x and y are required", op);
   if (!is_float_dtype(x->dtype) || y->dtype != x->dtype)
     return fail(L3D_E_DTYPE, "%s: x/y must share a float dtype", op);
   if (x->ndim != 4 || y->ndim != 4) return fail(L3D_E_SHAPE, "%s: x/y must be [B, L, H, D]", op);
@@ -565,7 +589,7 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
   p.theta = theta;
   p.scale = sqrtf(float(p.D));
   if (gamma) {
-    if (!gamma->data) return fail(L3D_E_NULL, "%s: gamma has no data", op);
+    if (no_data(gamma)) return fail(L3D_E_NULL, "%s: gamma has no data", op);
     if (gamma->dtype != L3D_F32) return fail(L3D_E_DTYPE, "%s: gamma must be F32", op);
     if (gamma->ndim != 2 || gamma->dims[0] != p.H || gamma->dims[1] != p.D)
       return fail(L3D_E_SHAPE, "%s: gamma must be [H, D]", op);
@@ -574,7 +598,7 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
     p.gsh = gamma->strides[0];
   }
   if (coords) {
-    if (!coords->data) return fail(L3D_E_NULL, "%s: coords has no data", op);
+    if (no_data(coords)) return fail(L3D_E_NULL, "%s: coords has no data", op);
     if (coords->dtype != L3D_I32 && coords->dtype != L3D_I64)
       return fail(L3D_E_DTYPE, "%s: coords must be I32/I64", op);
     if (coords->ndim != 2 || coords->dims[0] != p.L || coords->dims[1] != 3)
@@ -587,7 +611,7 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
     if (!gamma) return fail(L3D_E_NULL, "%s: nothing to do without gamma and coords", op);
   } else {
     for (const l3d_tensor* t : {cos_t, sin_t}) {
-      if (!t || !t->data) return fail(L3D_E_NULL, "%s: cos/sin tables are required", op);
+      if (!t || no_data(t)) return fail(L3D_E_NULL, "%s: cos/sin tables are required", op);
       if (t->dtype != L3D_F32) return fail(L3D_E_DTYPE, "%s: tables must be F32", op);
       if (t->ndim != 2 || t->dims[0] != p.L || t->dims[1] != p.D / 2)
         return fail(L3D_E_SHAPE, "%s: tables must be [L, D/2]", op);
@@ -646,7 +670,7 @@ extern "C" int l3d_rope3d_tables(const l3d_tensor* coords, int head_dim, float t
                                  const l3d_tensor* cos_out, const l3d_tensor* sin_out,
                                  l3d_stream stream) {
   const char* op = "l3d_rope3d_tables";
-  if (!coords || !cos_out || !sin_out || !coords->data || !cos_out->data || !sin_out->data)
+  if (!coords || !cos_out || !sin_out || no_data(coords) || no_data(cos_out) || no_data(sin_out))
     return fail(L3D_E_NULL, "%s: coords, cos and sin are required", op);
   if (head_dim <= 0 || head_dim % 2) return fail(L3D_E_SHAPE, "%s: head_dim must be even", op);
   const int fd = head_dim / 2 / 3;

@@ -240,16 +240,20 @@ extern "C" int l3d_sparse_neighbor_pairs(const l3d_tensor* coords, const l3d_ten
   const char* op = "l3d_sparse_neighbor_pairs";
   const l3d_tensor* req[] = {coords, pair_dest, pair_src, counts};
   for (const l3d_tensor* t : req)
-    if (!t || !t->data) return fail(L3D_E_NULL, "%s: coords, pair_dest, pair_src, counts required", op);
+    if (!t) return fail(L3D_E_NULL, "%s: coords, pair_dest, pair_src, counts required", op);
   for (const l3d_tensor* t : req)
     if (t->dtype != L3D_I32) return fail(L3D_E_DTYPE, "%s: all index tensors must be I32", op);
   if (coords->ndim != 2 || coords->dims[1] != 3) return fail(L3D_E_SHAPE, "%s: coords [N, 3]", op);
   const int64_t n = coords->dims[0];
+  // Empty coordinate lists (CoordMap::new(&[])) are valid; their views may
+  // carry no storage.  counts always needs storage.
+  if (no_data(counts) || (n > 0 && (no_data(coords) || no_data(pair_dest) || no_data(pair_src))))
+    return fail(L3D_E_NULL, "%s: null data pointer", op);
   if (n >= (int64_t(1) << 31)) return fail(L3D_E_UNSUPPORTED, "%s: N must fit in I32", op);
   for (const l3d_tensor* t : {pair_dest, pair_src}) {
     if (t->ndim != 2 || t->dims[0] != 27 || t->dims[1] != n)
       return fail(L3D_E_SHAPE, "%s: pair_dest/pair_src must be [27, N]", op);
-    if ((n > 1 && t->strides[1] != 1) || t->strides[0] != n)
+    if (n > 0 && ((n > 1 && t->strides[1] != 1) || t->strides[0] != n))
       return fail(L3D_E_ALIGN, "%s: pair tensors must be contiguous", op);
   }
   if (counts->ndim != 1 || counts->dims[0] != 27 || counts->strides[0] != 1)
@@ -295,7 +299,7 @@ extern "C" int l3d_sparse_neighbor_pairs(const l3d_tensor* coords, const l3d_ten
 extern "C" int l3d_index_select_rows(const l3d_tensor* feats, const l3d_tensor* ids,
                                      const l3d_tensor* out, l3d_stream stream) {
   const char* op = "l3d_index_select_rows";
-  if (!feats || !ids || !out || !feats->data || !ids->data || !out->data)
+  if (!feats || !ids || !out || no_data(feats) || no_data(ids) || no_data(out))
     return fail(L3D_E_NULL, "%s: feats, ids, out required", op);
   if (!is_float_dtype(feats->dtype) || out->dtype != feats->dtype)
     return fail(L3D_E_DTYPE, "%s: feats/out must share a float dtype", op);

@@ -22,7 +22,8 @@ def test_rope2d_tables(ops, orc, dev):
     import torch
 
     pos = vggt_positions(2, 37, 37)
-    c, s = ops.Rope2d(100.0).embeddings(torch.from_numpy(pos).to(dev), 64)
+    emb = ops.Rope2d(100.0).embeddings(torch.from_numpy(pos).to(dev), 64)
+    c, s = emb.cos_full, emb.sin_alt_full
     cr, sr = orc.rope2d_tables(pos, 100.0, 64)
     assert np.max(np.abs(c.cpu().numpy()[:, 0] - cr)) <= 2e-7
     assert np.max(np.abs(s.cpu().numpy()[:, 0] - sr)) <= 2e-7

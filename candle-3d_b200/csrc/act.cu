@@ -23,7 +23,7 @@ __global__ void __launch_bounds__(256) act_flat_kernel(const T* __restrict__ x, 
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) v[u][e] = act_f<A>(v[u][e]);
+      for (int e = 0; e < VEC; ++e) v[u][e] = act_t<A, (sizeof(T) == 2)>(v[u][e]);
       store_act<T, VEC>(y + (i + u * stride) * VEC, v[u]);
     }
   }
@@ -31,13 +31,13 @@ __global__ void __launch_bounds__(256) act_flat_kernel(const T* __restrict__ x, 
     float v[VEC];
     load_act<T, VEC>(x + i * VEC, v);
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) v[e] = act_f<A>(v[e]);
+    for (int e = 0; e < VEC; ++e) v[e] = act_t<A, (sizeof(T) == 2)>(v[e]);
     store_act<T, VEC>(y + i * VEC, v);
   }
   // Scalar tail (n not a multiple of VEC).
   if (VEC > 1 && blockIdx.x == 0) {
     for (int64_t j = nvec * VEC + threadIdx.x; j < n; j += blockDim.x)
-      y[j] = from_f<T>(act_f<A>(to_f(x[j])));
+      y[j] = from_f<T>(act_t<A, (sizeof(T) == 2)>(to_f(x[j])));
   }
 }
 
@@ -60,10 +60,10 @@ __global__ void __launch_bounds__(256) act_rows_kernel(const T* __restrict__ x, 
       float g[VEC];
       load_act<T, VEC>(xr + F + c, g);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) a[e] = a[e] * gelu_erf_f(g[e]);
+      for (int e = 0; e < VEC; ++e) a[e] = a[e] * act_t<ACT_GELU_ERF, (sizeof(T) == 2)>(g[e]);
     } else {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) a[e] = act_f<A>(a[e]);
+      for (int e = 0; e < VEC; ++e) a[e] = act_t<A, (sizeof(T) == 2)>(a[e]);
     }
     store_act<T, VEC>(y + row_offset(ym, r) + c, a);
   }

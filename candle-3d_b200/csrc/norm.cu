@@ -33,6 +33,7 @@ struct RowNormParams {
 };
 
 constexpr int kBlock = 256;
+constexpr int64_t kWaves = 4;  // grid cap in resident waves (grid-stride beyond)
 
 template <int G>
 __device__ __forceinline__ float group_sum(float v, float* red) {
@@ -57,36 +58,77 @@ __device__ __forceinline__ float group_sum(float v, float* red) {
   }
 }
 
-template <typename T, int VEC, int G, int kNV>
-__global__ void __launch_bounds__(kBlock) rownorm_kernel(const RowNormParams p) {
+// A row vector kept in registers in its storage format (one 16-byte pack, or
+// one float on the scalar path): half the registers of unpacked f32 for
+// 16-bit activations, so more rows are in flight per SM.
+template <typename T, int VEC> struct Packed { using S = uint4; };
+template <typename T> struct Packed<T, 1> { using S = float; };
+
+template <typename T, int VEC>
+__device__ __forceinline__ typename Packed<T, VEC>::S ld_packed(const T* p) {
+  if constexpr (VEC == 1) return to_f(p[0]);
+  else return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+template <typename T, int VEC>
+__device__ __forceinline__ void unpack_v(const typename Packed<T, VEC>::S& s, float (&f)[VEC]) {
+  if constexpr (VEC == 1) f[0] = s;
+  else unpack(s, f, T());
+}
+// Pack (rounding to the activation dtype).
+template <typename T, int VEC>
+__device__ __forceinline__ typename Packed<T, VEC>::S pack_v(const float (&f)[VEC]) {
+  if constexpr (VEC == 1) return to_f(from_f<T>(f[0]));
+  else return pack(f, T());
+}
+template <typename T, int VEC>
+__device__ __forceinline__ void st_packed(T* p, const typename Packed<T, VEC>::S& s) {
+  if constexpr (VEC == 1) p[0] = from_f<T>(s);
+  else __stcs(reinterpret_cast<uint4*>(p), s);
+}
+
+// RES: the residual branch is present (x and h both held in registers).
+template <typename T, int VEC, int G, int kNV, bool RES>
+__global__ void __launch_bounds__(kBlock, RES ? 2 : (kNV <= 4 ? 4 : 3))
+    rownorm_kernel(const RowNormParams p) {
+  using S = typename Packed<T, VEC>::S;
   __shared__ float red[kBlock / 32];
   constexpr int RPB = kBlock / G;  // rows per block
   const int tid = threadIdx.x % G;
-  const int64_t row = int64_t(blockIdx.x) * RPB + threadIdx.x / G;
-  const bool valid = row < p.rows;
   const int64_t nvec = p.C / VEC;
+  // Grid-stride over groups of RPB rows; the trip count is uniform per block
+  // (the cross-warp reductions synchronise the whole block).
+  for (int64_t row0 = int64_t(blockIdx.x) * RPB; row0 < p.rows;
+       row0 += int64_t(gridDim.x) * RPB) {
+  const int64_t row = row0 + threadIdx.x / G;
+  const bool valid = row < p.rows;
   const int64_t b = valid ? row / p.rows_per_batch : 0;
 
   const T* xr = static_cast<const T*>(p.x) + (valid ? row_offset(p.xm, row) : 0);
-  float v[kNV][VEC];
+  S v[kNV];
 #pragma unroll
   for (int i = 0; i < kNV; ++i) {
     const int64_t vi = tid + int64_t(i) * G;
-    if (valid && vi < nvec) load_act<T, VEC>(xr + vi * VEC, v[i]);
-    else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) v[i][e] = 0.f;
-    }
+    if (valid && vi < nvec) v[i] = ld_packed<T, VEC>(xr + vi * VEC);
+    else v[i] = S{};  // all-zero bits: 0.0 in every float dtype
   }
-  // Residual branch: r = x + g1 * h.
-  if (p.h) {
+  // Residual branch: r = x + g1 * h, rounded to the activation dtype exactly as
+  // it is stored, so the norm sees the values a later reader of r sees.
+  if constexpr (RES) {
     const T* hr = static_cast<const T*>(p.h) + (valid ? row_offset(p.hm, row) : 0);
+    T* rr = p.r_out ? static_cast<T*>(p.r_out) + (valid ? row_offset(p.rm, row) : 0) : nullptr;
+    S hp[kNV];
+#pragma unroll
+    for (int i = 0; i < kNV; ++i) {
+      const int64_t vi = tid + int64_t(i) * G;
+      if (valid && vi < nvec) hp[i] = ld_packed<T, VEC>(hr + vi * VEC);
+    }
 #pragma unroll
     for (int i = 0; i < kNV; ++i) {
       const int64_t vi = tid + int64_t(i) * G;
       if (valid && vi < nvec) {
-        float hv[VEC];
-        load_act<T, VEC>(hr + vi * VEC, hv);
+        float a[VEC], hv[VEC];
+        unpack_v<T, VEC>(v[i], a);
+        unpack_v<T, VEC>(hp[i], hv);
         if (p.g1.ptr) {
           float g[VEC];
           load_chan<VEC>(p.g1, b, vi * VEC, g);
@@ -94,24 +136,9 @@ __global__ void __launch_bounds__(kBlock) rownorm_kernel(const RowNormParams p) 
           for (int e = 0; e < VEC; ++e) hv[e] = hv[e] * g[e];
         }
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) v[i][e] = v[i][e] + hv[e];
-      }
-    }
-    if (p.r_out) {
-      T* rr = static_cast<T*>(p.r_out) + (valid ? row_offset(p.rm, row) : 0);
-#pragma unroll
-      for (int i = 0; i < kNV; ++i) {
-        const int64_t vi = tid + int64_t(i) * G;
-        if (valid && vi < nvec) {
-          // Round the residual exactly as it is stored, so y is computed from
-          // the same values a later reader of r_out sees.
-          float t[VEC];
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) t[e] = to_f(from_f<T>(v[i][e]));
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) v[i][e] = t[e];
-          store_act<T, VEC>(rr + vi * VEC, v[i]);
-        }
+        for (int e = 0; e < VEC; ++e) a[e] = a[e] + hv[e];
+        v[i] = pack_v<T, VEC>(a);
+        if (rr) st_packed<T, VEC>(rr + vi * VEC, v[i]);
       }
     }
   }
@@ -120,9 +147,12 @@ __global__ void __launch_bounds__(kBlock) rownorm_kernel(const RowNormParams p) 
   if (p.norm == NORM_LAYER) {
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < kNV; ++i)
+    for (int i = 0; i < kNV; ++i) {
+      float a[VEC];
+      unpack_v<T, VEC>(v[i], a);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) s += v[i][e];
+      for (int e = 0; e < VEC; ++e) s += a[e];
+    }
     s = group_sum<G>(s, red);
     mean = s / float(p.C);
     float ss = 0.f;
@@ -130,9 +160,11 @@ __global__ void __launch_bounds__(kBlock) rownorm_kernel(const RowNormParams p) 
     for (int i = 0; i < kNV; ++i) {
       const int64_t vi = tid + int64_t(i) * G;
       if (vi < nvec) {
+        float a[VEC];
+        unpack_v<T, VEC>(v[i], a);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
-          const float d = v[i][e] - mean;
+          const float d = a[e] - mean;
           ss += d * d;
         }
       }
@@ -142,69 +174,97 @@ __global__ void __launch_bounds__(kBlock) rownorm_kernel(const RowNormParams p) 
   } else if (p.norm == NORM_RMS) {
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < kNV; ++i)
+    for (int i = 0; i < kNV; ++i) {
+      float a[VEC];
+      unpack_v<T, VEC>(v[i], a);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) ss += v[i][e] * v[i][e];
+      for (int e = 0; e < VEC; ++e) ss += a[e] * a[e];
+    }
     ss = group_sum<G>(ss, red);
     inv = 1.f / sqrtf(ss / float(p.C) + p.eps);
   }
-  if (!valid) return;
+  if (!valid) continue;
 
   T* yr = static_cast<T*>(p.y) + row_offset(p.ym, row);
 #pragma unroll
   for (int i = 0; i < kNV; ++i) {
     const int64_t vi = tid + int64_t(i) * G;
     if (vi >= nvec) continue;
-    const int64_t c0 = vi * VEC;
-    float o[VEC];
     if (p.norm == NORM_NONE) {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] = v[i][e];
-    } else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] = (v[i][e] - mean) * inv;
-      float t[VEC];
-      if (p.w.ptr) {
-        load_chan<VEC>(p.w, 0, c0, t);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = o[e] * t[e];
-      }
-      if (p.b.ptr) {
-        load_chan<VEC>(p.b, 0, c0, t);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = o[e] + t[e];
-      }
-      if (p.scale.ptr) {
-        load_chan<VEC>(p.scale, b, c0, t);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = o[e] * (1.f + t[e]);
-      }
-      if (p.shift.ptr) {
-        load_chan<VEC>(p.shift, b, c0, t);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = o[e] + t[e];
-      }
-      if (p.g2.ptr) {
-        load_chan<VEC>(p.g2, b, c0, t);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = t[e] * o[e];
-      }
-      if (p.add_input) {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = o[e] + v[i][e];
-      }
+      st_packed<T, VEC>(yr + vi * VEC, v[i]);
+      continue;
     }
-    store_act<T, VEC>(yr + c0, o);
+    const int64_t c0 = vi * VEC;
+    float a[VEC], o[VEC], t[VEC];
+    unpack_v<T, VEC>(v[i], a);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) o[e] = (a[e] - mean) * inv;
+    if (p.w.ptr) {
+      load_chan<VEC>(p.w, 0, c0, t);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = o[e] * t[e];
+    }
+    if (p.b.ptr) {
+      load_chan<VEC>(p.b, 0, c0, t);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = o[e] + t[e];
+    }
+    if (p.scale.ptr) {
+      load_chan<VEC>(p.scale, b, c0, t);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = o[e] * (1.f + t[e]);
+    }
+    if (p.shift.ptr) {
+      load_chan<VEC>(p.shift, b, c0, t);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = o[e] + t[e];
+    }
+    if (p.g2.ptr) {
+      load_chan<VEC>(p.g2, b, c0, t);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = t[e] * o[e];
+    }
+    if (p.add_input) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = o[e] + a[e];
+    }
+    st_packed<T, VEC>(yr + c0, pack_v<T, VEC>(o));
   }
+  }
+}
+
+// Resident blocks of one kernel instance on the whole device (one full wave).
+template <typename T, int VEC, int G, int NV, bool RES>
+static int64_t rownorm_wave() {
+  static const int64_t wave = [] {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rownorm_kernel<T, VEC, G, NV, RES>,
+                                                      kBlock, 0) != cudaSuccess || n < 1)
+      n = 1;
+    return int64_t(n) * sm_count();
+  }();
+  return wave;
+}
+
+template <typename T, int VEC, int G, int NV, bool RES>
+static void launch_rownorm_k(const RowNormParams& p, cudaStream_t s) {
+  constexpr int rpb = kBlock / G;
+  int64_t blocks = (p.rows + rpb - 1) / rpb;
+  // Persistent: at most kWaves resident waves of blocks, each block striding
+  // over row groups.
+  const int64_t cap = kWaves * rownorm_wave<T, VEC, G, NV, RES>();
+  if (blocks > cap) blocks = cap;
+  rownorm_kernel<T, VEC, G, NV, RES><<<dim3(unsigned(blocks)), kBlock, 0, s>>>(p);
 }
 
 template <typename T, int VEC, int NV>
 static void launch_rownorm_g(const RowNormParams& p, int G, cudaStream_t s) {
-  const int rpb = kBlock / G;
-  const int64_t blocks = (p.rows + rpb - 1) / rpb;
   switch (G) {
-#define L3D_CASE(GG)                                                                      \
-  case GG: rownorm_kernel<T, VEC, GG, NV><<<dim3((unsigned)blocks), kBlock, 0, s>>>(p); break;
+#define L3D_CASE(GG)                                        \
+  case GG:                                                  \
+    if (p.h) launch_rownorm_k<T, VEC, GG, NV, true>(p, s);  \
+    else launch_rownorm_k<T, VEC, GG, NV, false>(p, s);     \
+    break;
     L3D_CASE(8) L3D_CASE(16) L3D_CASE(32) L3D_CASE(64) L3D_CASE(128) L3D_CASE(256)
 #undef L3D_CASE
     default: break;
@@ -364,7 +424,7 @@ extern "C" int l3d_layer_norm_modulate(const l3d_tensor* x, const l3d_tensor* we
 extern "C" int l3d_gated_residual(const l3d_tensor* x, const l3d_tensor* h,
                                   const l3d_tensor* gate, const l3d_tensor* out,
                                   l3d_stream stream) {
-  if (!h || !gate) return fail(L3D_E_NULL, "l3d_gated_residual: h and gate are required");
+  if (!h) return fail(L3D_E_NULL, "l3d_gated_residual: h is required");  // gate NULL: x + h
   RowNormArgs a{};
   a.x = x; a.h = h; a.g1 = gate; a.y = out;
   a.norm = NORM_NONE; a.op = "l3d_gated_residual"; a.batch_dims = 1;

@@ -246,12 +246,40 @@ struct Rope3dParams {
   int64_t tcbase, tcsl, tsbase, tssl;
 };
 
+// 8 consecutive elements in their storage format (16 B for 16-bit types,
+// 32 B for f32), unpacked only where the arithmetic needs them.
+template <typename T>
+struct Pack8 {
+  uint4 u[sizeof(T) == 4 ? 2 : 1];
+};
+template <typename T>
+__device__ __forceinline__ Pack8<T> ld_pack8(const T* p) {
+  Pack8<T> r;
+  r.u[0] = __ldcs(reinterpret_cast<const uint4*>(p));
+  if constexpr (sizeof(T) == 4) r.u[1] = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void unpack8(const Pack8<T>& r, float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    float a[4], b[4];
+    unpack(r.u[0], a, float());
+    unpack(r.u[1], b, float());
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { f[i] = a[i]; f[4 + i] = b[i]; }
+  } else {
+    unpack(r.u[0], f, T());
+  }
+}
+
 // EPL elements per lane (8: 16-byte path; 2: one pair per lane), LPH lanes per
-// head row (D / EPL rounded up to a power of two).
+// head row (D / EPL rounded up to a power of two).  gamma * sqrt(D) is staged
+// once per block in shared memory (dynamic, H * D floats) when present.
 template <typename T, int EPL, int LPH>
-__global__ void __launch_bounds__(256) rope3d_kernel(const Rope3dParams p) {
-  constexpr int NP = EPL / 2;        // pairs per lane
-  constexpr int HPI = 32 / LPH;      // heads per warp iteration
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2) rope3d_kernel(const Rope3dParams p) {
+  extern __shared__ float gsm[];  // [H, D] gamma * sqrt(D)
+  constexpr int NP = EPL / 2;     // pairs per lane
+  constexpr int HPI = 32 / LPH;   // heads per warp iteration
   const int lane = threadIdx.x & 31;
   const int m = lane % LPH;
   const int hg = lane / LPH;
@@ -260,6 +288,14 @@ __global__ void __launch_bounds__(256) rope3d_kernel(const Rope3dParams p) {
   const int64_t tokens = p.B * p.L;
   const int half = p.D / 2;
   const bool lane_on = m * EPL < p.D;
+
+  if (p.gamma) {
+    for (int i = threadIdx.x; i < p.H * p.D; i += blockDim.x) {
+      const int h = i / p.D, d = i - h * p.D;
+      gsm[i] = p.gamma[int64_t(h) * p.gsh + d] * p.scale;
+    }
+    __syncthreads();
+  }
 
   // Frequencies of this lane's pairs (constant across tokens).
   float fr[NP];
@@ -277,6 +313,8 @@ __global__ void __launch_bounds__(256) rope3d_kernel(const Rope3dParams p) {
   for (int64_t tok = warp0; tok < tokens; tok += nwarps) {
     const int64_t b = tok / p.L;
     const int64_t l = tok - b * p.L;
+    const T* xt = static_cast<const T*>(p.x) + p.xbase + b * p.xsb + l * p.xsl + m * EPL;
+    T* yt = static_cast<T*>(p.y) + p.ybase + b * p.ysb + l * p.ysl + m * EPL;
     float cs[NP], sn[NP];
     if (p.use_table) {
 #pragma unroll
@@ -299,58 +337,68 @@ __global__ void __launch_bounds__(256) rope3d_kernel(const Rope3dParams p) {
         }
       }
     }
-    // Heads in groups of MAXIT warp iterations: all loads of a group are issued
-    // before any arithmetic, so a warp keeps up to MAXIT x 512 B in flight.
+    // Heads in groups of MAXIT warp iterations: the group's loads are all
+    // issued (kept packed) before any arithmetic.
     constexpr int MAXIT = 8;
     for (int hb = 0; hb < p.H; hb += HPI * MAXIT) {
-    float vv[MAXIT][EPL];
+      Pack8<T> pk[EPL == 8 ? MAXIT : 1];
+      float sv[EPL == 8 ? 1 : MAXIT][2];
 #pragma unroll
-    for (int it = 0; it < MAXIT; ++it) {
-      const int h = hb + it * HPI + hg;
-      const T* src = static_cast<const T*>(p.x) + p.xbase + b * p.xsb + l * p.xsl +
-                     int64_t(h) * p.xsh + m * EPL;
-      if (h < p.H && lane_on) {
-        if constexpr (EPL == 8) load8<T>(src, vv[it]);
-        else { vv[it][0] = to_f(src[0]); vv[it][1] = to_f(src[1]); }
-      } else {
-#pragma unroll
-        for (int i = 0; i < EPL; ++i) vv[it][i] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int it = 0; it < MAXIT; ++it) {
-      if (hb + it * HPI >= p.H) break;  // warp-uniform
-      const int h = hb + it * HPI + hg;
-      const bool valid = h < p.H && lane_on;
-      float* v = vv[it];
-      if (p.gamma) {
-        float ss = 0.f;
-#pragma unroll
-        for (int i = 0; i < EPL; ++i) ss += v[i] * v[i];
-#pragma unroll
-        for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float nrm = fminf(fmaxf(sqrtf(ss), 1e-12f), 1e30f);
-        const float rn = 1.f / nrm;
-        if (valid) {
-          const float* g = p.gamma + int64_t(h) * p.gsh + m * EPL;
-#pragma unroll
-          for (int i = 0; i < EPL; ++i) v[i] = v[i] * rn * __ldg(g + i) * p.scale;
+      for (int it = 0; it < MAXIT; ++it) {
+        const int h = hb + it * HPI + hg;
+        const T* src = xt + int64_t(h) * p.xsh;
+        const bool on = h < p.H && lane_on;
+        if constexpr (EPL == 8) {
+          if (on) pk[it] = ld_pack8<T>(src);
+          else pk[it] = Pack8<T>{};
+        } else {
+          sv[it][0] = on ? to_f(src[0]) : 0.f;
+          sv[it][1] = on ? to_f(src[1]) : 0.f;
         }
       }
-      float o[EPL];
 #pragma unroll
-      for (int k = 0; k < NP; ++k) {
-        const float re = v[2 * k], im = v[2 * k + 1];
-        o[2 * k] = re * cs[k] - im * sn[k];
-        o[2 * k + 1] = re * sn[k] + im * cs[k];
+      for (int it = 0; it < MAXIT; ++it) {
+        if (hb + it * HPI >= p.H) break;  // warp-uniform
+        const int h = hb + it * HPI + hg;
+        const bool valid = h < p.H && lane_on;
+        float v[EPL];
+        if constexpr (EPL == 8) unpack8<T>(pk[it], v);
+        else { v[0] = sv[it][0]; v[1] = sv[it][1]; }
+        if (p.gamma) {
+          float ss = 0.f;
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) ss += v[i] * v[i];
+#pragma unroll
+          for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          const float rn = 1.f / fminf(fmaxf(sqrtf(ss), 1e-12f), 1e30f);
+          if (valid) {
+            const float* g = gsm + h * p.D + m * EPL;
+            float gv[EPL];
+            if constexpr (EPL == 8) {
+              const float4 g0 = reinterpret_cast<const float4*>(g)[0];
+              const float4 g1 = reinterpret_cast<const float4*>(g)[1];
+              gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+              gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+            } else {
+              gv[0] = g[0]; gv[1] = g[1];
+            }
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) v[i] = v[i] * rn * gv[i];
+          }
+        }
+        float o[EPL];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+          const float re = v[2 * k], im = v[2 * k + 1];
+          o[2 * k] = re * cs[k] - im * sn[k];
+          o[2 * k + 1] = re * sn[k] + im * cs[k];
+        }
+        if (valid) {
+          T* dst = yt + int64_t(h) * p.ysh;
+          if constexpr (EPL == 8) store8<T>(dst, o);
+          else { dst[0] = from_f<T>(o[0]); dst[1] = from_f<T>(o[1]); }
+        }
       }
-      if (valid) {
-        T* dst = static_cast<T*>(p.y) + p.ybase + b * p.ysb + l * p.ysl + int64_t(h) * p.ysh +
-                 m * EPL;
-        if constexpr (EPL == 8) store8<T>(dst, o);
-        else { dst[0] = from_f<T>(o[0]); dst[1] = from_f<T>(o[1]); }
-      }
-    }
     }
   }
 }
@@ -625,15 +673,17 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
   }
   if (p.B * p.L == 0 || p.H == 0) return L3D_OK;
   const bool fast = (p.D % 8 == 0) && p.D <= 256 && aligned_view16(x) && aligned_view16(y);
+  const size_t smem = p.gamma ? size_t(p.H) * size_t(p.D) * sizeof(float) : 0;
+  if (smem > 48 * 1024) return fail(L3D_E_UNSUPPORTED, "%s: gamma [H, D] above 12288 values", op);
   const int blocks = launch_grid_warps(p.B * p.L);
   if (fast) {
     const int lph = p.D / 8 <= 4 ? 4 : p.D / 8 <= 8 ? 8 : p.D / 8 <= 16 ? 16 : 32;
     L3D_DISPATCH_FLOAT(x->dtype, T, {
       switch (lph) {
-        case 4: rope3d_kernel<T, 8, 4><<<blocks, 256, 0, stream>>>(p); break;
-        case 8: rope3d_kernel<T, 8, 8><<<blocks, 256, 0, stream>>>(p); break;
-        case 16: rope3d_kernel<T, 8, 16><<<blocks, 256, 0, stream>>>(p); break;
-        default: rope3d_kernel<T, 8, 32><<<blocks, 256, 0, stream>>>(p); break;
+        case 4: rope3d_kernel<T, 8, 4><<<blocks, 256, smem, stream>>>(p); break;
+        case 8: rope3d_kernel<T, 8, 8><<<blocks, 256, smem, stream>>>(p); break;
+        case 16: rope3d_kernel<T, 8, 16><<<blocks, 256, smem, stream>>>(p); break;
+        default: rope3d_kernel<T, 8, 32><<<blocks, 256, smem, stream>>>(p); break;
       }
     });
   } else {
@@ -642,10 +692,10 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
     const int lph = pairs <= 4 ? 4 : pairs <= 8 ? 8 : pairs <= 16 ? 16 : 32;
     L3D_DISPATCH_FLOAT(x->dtype, T, {
       switch (lph) {
-        case 4: rope3d_kernel<T, 2, 4><<<blocks, 256, 0, stream>>>(p); break;
-        case 8: rope3d_kernel<T, 2, 8><<<blocks, 256, 0, stream>>>(p); break;
-        case 16: rope3d_kernel<T, 2, 16><<<blocks, 256, 0, stream>>>(p); break;
-        default: rope3d_kernel<T, 2, 32><<<blocks, 256, 0, stream>>>(p); break;
+        case 4: rope3d_kernel<T, 2, 4><<<blocks, 256, smem, stream>>>(p); break;
+        case 8: rope3d_kernel<T, 2, 8><<<blocks, 256, smem, stream>>>(p); break;
+        case 16: rope3d_kernel<T, 2, 16><<<blocks, 256, smem, stream>>>(p); break;
+        default: rope3d_kernel<T, 2, 32><<<blocks, 256, smem, stream>>>(p); break;
       }
     });
   }

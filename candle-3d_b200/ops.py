@@ -55,8 +55,8 @@ def layer_norm_modulate(x, shift=None, scale=None, gate=None, add_input=False, w
     return y
 
 
-def gated_residual(x, h, gate):
-    """x + h * gate (crate/runtime/trellis2_blocks.rs:632-633)."""
+def gated_residual(x, h, gate=None):
+    """x + h * gate (crate/runtime/trellis2_blocks.rs:632-633); gate None: x + h."""
     _check_cuda(x, h, gate)
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     call("l3d_gated_residual", ref(desc(x)), ref(desc(h)), ref(desc(gate)), ref(desc(out)), _s(x))

@@ -109,7 +109,8 @@ int l3d_layer_norm_modulate(const l3d_tensor* x, const l3d_tensor* weight,
                             const l3d_tensor* scale, const l3d_tensor* gate, int add_input,
                             float eps, const l3d_tensor* y, l3d_stream stream);
 
-/* Gated residual: out = x + gate * h, gate [B, C] / [B, 1, C] / [C].
+/* Gated residual: out = x + gate * h, gate [B, C] / [B, 1, C] / [C], or NULL
+ * for the plain residual add out = x + h.
  * Replaces `xs.add(h.broadcast_mul(gate))` crate/runtime/trellis2_blocks.rs:632-633,
  * 644-645,708-709,716-717. */
 int l3d_gated_residual(const l3d_tensor* x, const l3d_tensor* h, const l3d_tensor* gate,

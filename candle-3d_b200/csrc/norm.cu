@@ -33,7 +33,7 @@ struct RowNormParams {
 };
 
 constexpr int kBlock = 256;
-constexpr int64_t kWaves = 4;  // grid cap in resident waves (grid-stride beyond)
+constexpr int64_t kWaves = 2;  // grid cap in resident waves (grid-stride beyond)
 
 template <int G>
 __device__ __forceinline__ float group_sum(float v, float* red) {
@@ -88,28 +88,43 @@ __device__ __forceinline__ void st_packed(T* p, const typename Packed<T, VEC>::S
 
 // RES: the residual branch is present (x and h both held in registers).
 template <typename T, int VEC, int G, int kNV, bool RES>
-__global__ void __launch_bounds__(kBlock, RES ? 2 : (kNV <= 4 ? 4 : 3))
+__global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
     rownorm_kernel(const RowNormParams p) {
   using S = typename Packed<T, VEC>::S;
   __shared__ float red[kBlock / 32];
   constexpr int RPB = kBlock / G;  // rows per block
   const int tid = threadIdx.x % G;
   const int64_t nvec = p.C / VEC;
+  const int64_t stride = int64_t(gridDim.x) * RPB;
+  // Load row r's vectors of this thread (zeros past the row / past the end).
+  auto load_x = [&](S (&dst)[kNV], int64_t r) {
+    const bool ok = r < p.rows;
+    const T* xr = static_cast<const T*>(p.x) + (ok ? row_offset(p.xm, r) : 0);
+#pragma unroll
+    for (int i = 0; i < kNV; ++i) {
+      const int64_t vi = tid + int64_t(i) * G;
+      if (ok && vi < nvec) dst[i] = ld_packed<T, VEC>(xr + vi * VEC);
+      else dst[i] = S{};  // all-zero bits: 0.0 in every float dtype
+    }
+  };
+  // Without a residual branch the next row of this thread group is prefetched
+  // while the current one is reduced and written, so loads stay in flight.
+  S pf[RES ? 1 : kNV];
+  if constexpr (!RES) load_x(pf, int64_t(blockIdx.x) * RPB + threadIdx.x / G);
   // Grid-stride over groups of RPB rows; the trip count is uniform per block
   // (the cross-warp reductions synchronise the whole block).
-  for (int64_t row0 = int64_t(blockIdx.x) * RPB; row0 < p.rows;
-       row0 += int64_t(gridDim.x) * RPB) {
+  for (int64_t row0 = int64_t(blockIdx.x) * RPB; row0 < p.rows; row0 += stride) {
   const int64_t row = row0 + threadIdx.x / G;
   const bool valid = row < p.rows;
   const int64_t b = valid ? row / p.rows_per_batch : 0;
 
-  const T* xr = static_cast<const T*>(p.x) + (valid ? row_offset(p.xm, row) : 0);
   S v[kNV];
+  if constexpr (RES) {
+    load_x(v, row);
+  } else {
 #pragma unroll
-  for (int i = 0; i < kNV; ++i) {
-    const int64_t vi = tid + int64_t(i) * G;
-    if (valid && vi < nvec) v[i] = ld_packed<T, VEC>(xr + vi * VEC);
-    else v[i] = S{};  // all-zero bits: 0.0 in every float dtype
+    for (int i = 0; i < kNV; ++i) v[i] = pf[i];
+    if (row0 + stride < p.rows) load_x(pf, row + stride);
   }
   // Residual branch: r = x + g1 * h, rounded to the activation dtype exactly as
   // it is stored, so the norm sees the values a later reader of r sees.

@@ -21,7 +21,10 @@ def test_vggt_stack_matches_reference(pkg, dev):
 
     from candle3d_b200 import blocks
 
-    agg = blocks.VggtAggregator(depth=2, device=dev)
+    # LayerScale 1.0 instead of the 0.01 init: with 0.01 the per-block update
+    # is far below one bf16 ulp of the residual stream and rounds away (in
+    # Candle's bf16 path as well), leaving nothing to compare.
+    agg = blocks.VggtAggregator(depth=2, device=dev, ls_init=1.0)
     B, S, ph, pw, special = 1, 2, 9, 9, 5
     N = special + ph * pw
     fpos = blocks.VggtAggregator.positions(B, S, ph, pw, special, dev)

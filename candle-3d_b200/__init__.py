@@ -3,8 +3,8 @@ candle-3d models behind a C ABI (libl3dops.so, include/l3d_ops.h).
 
 `ops` mirrors the Candle ops the reference model code calls; `_lib` is the
 ctypes binding of the C ABI; `blocks` assembles the VGGT, TripoSG and
-TRELLIS.2 block stacks from them.
+TRELLIS.2 block stacks from them; `shard` splits token rows across ranks.
 """
-from . import _lib, blocks, ops  # noqa: F401
+from . import _lib, blocks, ops, shard  # noqa: F401
 
-__all__ = ["ops", "blocks", "_lib"]
+__all__ = ["ops", "blocks", "shard", "_lib"]

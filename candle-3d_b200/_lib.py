@@ -101,6 +101,7 @@ _SIGS = {
                             C.c_size_t, _S], C.c_int),
     "l3d_sparse_neighbor_pairs_workspace_size": ([C.c_int64], C.c_size_t),
     "l3d_sparse_neighbor_pairs": ([_P, _P, _P, _P, C.c_void_p, C.c_size_t, _S], C.c_int),
+    "l3d_sparse_neighbor_pairs_noalloc": ([_P, _P, _P, _P, _S], C.c_int),
     "l3d_index_select_rows": ([_P, _P, _P, _S], C.c_int),
 }
 

@@ -12,6 +12,8 @@
 //   4. recompute the lookups and write (dest, src) pairs at their scanned
 //      positions, so each offset's pairs come out in ascending dest order,
 //      bit-identical to the reference loop.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace l3d {
@@ -333,5 +335,113 @@ extern "C" int l3d_index_select_rows(const l3d_tensor* feats, const l3d_tensor* 
           static_cast<const int32_t*>(ids->data) + ids->offset, ids->strides[0], o,
           out->strides[0], n, C);
   });
+  return check_launch(op);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of l3d_sparse_neighbor_pairs.
+//
+// Some callers cannot hand the library a workspace: a Candle `CustomOp`
+// whose `cuda_fwd` only receives the input storages and returns one output
+// allocation, a CUDA-graph replay whose buffers were fixed at capture, or a
+// host runtime that forbids device allocation on its inference path.  For
+// them the hash table and tile counts live in this file-scope device array,
+// sized for at most kNoAllocMaxCoords coordinates.  Every GPU that loads the
+// library holds the array until the process exits.
+namespace l3d {
+constexpr int64_t kNoAllocMaxCoords = 65536;
+constexpr size_t kNoAllocCap = 131072;  // table slots for the maximum (>= 2N, power of two)
+constexpr size_t kNoAllocTiles = (kNoAllocMaxCoords + kTile - 1) / kTile;
+constexpr size_t kNoAllocBytes = ((kNoAllocCap * 8 + 255) & ~size_t(255)) +
+                                 ((kNoAllocCap * 4 + 255) & ~size_t(255)) +
+                                 ((27 * kNoAllocTiles * 4 + 255) & ~size_t(255));
+static __device__ __align__(256) unsigned char g_pairs_scratch[kNoAllocBytes];
+
+// Device address of g_pairs_scratch on the current device.  The host-side name
+// of the array is only a stand-in for it, so the address is looked up once per
+// device (with that device current) and cached.
+static int pairs_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(L3D_E_CUDA, "l3d_sparse_neighbor_pairs_noalloc: no current device");
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_pairs_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(L3D_E_CUDA, "l3d_sparse_neighbor_pairs_noalloc: cudaGetSymbolAddress: %s",
+                  cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return L3D_OK;
+}
+}  // namespace l3d
+
+extern "C" int l3d_sparse_neighbor_pairs_noalloc(const l3d_tensor* coords,
+                                                 const l3d_tensor* pair_dest,
+                                                 const l3d_tensor* pair_src,
+                                                 const l3d_tensor* counts, l3d_stream stream) {
+  const char* op = "l3d_sparse_neighbor_pairs_noalloc";
+  const l3d_tensor* req[] = {coords, pair_dest, pair_src, counts};
+  for (const l3d_tensor* t : req)
+    if (!t) return fail(L3D_E_NULL, "%s: coords, pair_dest, pair_src, counts required", op);
+  for (const l3d_tensor* t : req)
+    if (t->dtype != L3D_I32) return fail(L3D_E_DTYPE, "%s: all index tensors must be I32", op);
+  if (coords->ndim != 2 || coords->dims[1] != 3) return fail(L3D_E_SHAPE, "%s: coords [N, 3]", op);
+  const int64_t n = coords->dims[0];
+  if (n > kNoAllocMaxCoords)
+    return fail(L3D_E_UNSUPPORTED,
+                "%s: %lld coordinates exceed the fixed scratch limit of %lld; use "
+                "l3d_sparse_neighbor_pairs with a workspace",
+                op, (long long)n, (long long)kNoAllocMaxCoords);
+  if (no_data(counts) || (n > 0 && (no_data(coords) || no_data(pair_dest) || no_data(pair_src))))
+    return fail(L3D_E_NULL, "%s: null data pointer", op);
+  for (const l3d_tensor* t : {pair_dest, pair_src}) {
+    if (t->ndim != 2 || t->dims[0] != 27 || t->dims[1] != n)
+      return fail(L3D_E_SHAPE, "%s: pair_dest/pair_src must be [27, N]", op);
+    if (n > 0 && ((n > 1 && t->strides[1] != 1) || t->strides[0] != n))
+      return fail(L3D_E_ALIGN, "%s: pair tensors must be contiguous", op);
+  }
+  if (counts->ndim != 1 || counts->dims[0] != 27 || counts->strides[0] != 1)
+    return fail(L3D_E_SHAPE, "%s: counts must be contiguous [27]", op);
+  void* scratch = nullptr;
+  int rc = pairs_scratch_address(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int32_t* cnt = static_cast<int32_t*>(counts->data) + counts->offset;
+  if (n == 0) {
+    if (cudaMemsetAsync(cnt, 0, 27 * sizeof(int32_t), s) != cudaSuccess)
+      return fail(L3D_E_CUDA, "%s: memset failed", op);
+    return L3D_OK;
+  }
+  // Same passes as l3d_sparse_neighbor_pairs, over the fixed scratch array.
+  // The table is cleared on every call (the array keeps the previous call's
+  // contents); the tile counts are fully rewritten by the count pass.
+  SparseWs ws;
+  ws.cap = table_cap(n);
+  ws.tiles = (n + kTile - 1) / kTile;
+  char* base = static_cast<char*>(scratch);
+  ws.keys = reinterpret_cast<unsigned long long*>(base);
+  base += align256(ws.cap * 8);
+  ws.vals = reinterpret_cast<int32_t*>(base);
+  base += align256(ws.cap * 4);
+  ws.tile_counts = reinterpret_cast<int32_t*>(base);
+  if (cudaMemsetAsync(ws.keys, 0xff, ws.cap * 8, s) != cudaSuccess ||
+      cudaMemsetAsync(ws.vals, 0xff, ws.cap * 4, s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: scratch clear failed", op);
+  const int32_t* cp = static_cast<const int32_t*>(coords->data) + coords->offset;
+  const int64_t cs0 = coords->strides[0], cs1 = coords->strides[1];
+  const int blocks = int((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  hash_insert_kernel<<<blocks, 256, 0, s>>>(cp, cs0, cs1, n, ws);
+  const dim3 grid(unsigned(ws.tiles), 27);
+  pair_count_kernel<<<grid, kTile, 0, s>>>(cp, cs0, cs1, n, ws);
+  pair_scan_kernel<<<27, 1024, 0, s>>>(ws, cnt);
+  pair_write_kernel<<<grid, kTile, 0, s>>>(cp, cs0, cs1, n, ws,
+                                           static_cast<int32_t*>(pair_dest->data) + pair_dest->offset,
+                                           static_cast<int32_t*>(pair_src->data) + pair_src->offset,
+                                           n);
   return check_launch(op);
 }

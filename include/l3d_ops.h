@@ -291,6 +291,22 @@ int l3d_sparse_neighbor_pairs(const l3d_tensor* coords, const l3d_tensor* pair_d
                               const l3d_tensor* pair_src, const l3d_tensor* counts,
                               void* workspace, size_t workspace_bytes, l3d_stream stream);
 
+/* Same result as l3d_sparse_neighbor_pairs, for callers that cannot allocate
+ * device memory (a Candle CustomOp's cuda_fwd, a replayed CUDA graph, a host
+ * runtime that forbids allocation while serving): takes no workspace and
+ * allocates nothing.  No counterpart in the reference (its CoordMap is a
+ * host HashMap).  Scratch is a file-scope device array of the library sized
+ * for at most 65536 coordinates (about 1.6 MB, held on every GPU that loads
+ * the library until the process exits); larger inputs are rejected with
+ * L3D_E_UNSUPPORTED.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (different streams, or different host threads) race and must be
+ * serialised by the caller. */
+int l3d_sparse_neighbor_pairs_noalloc(const l3d_tensor* coords, const l3d_tensor* pair_dest,
+                                      const l3d_tensor* pair_src, const l3d_tensor* counts,
+                                      l3d_stream stream);
+
 /* index_select_rows crate/runtime/trellis2_sparse.rs:118-133:
  * out[j, :] = feats[ids[j], :]; ids I32/U32/I64; feats/out same dtype. */
 int l3d_index_select_rows(const l3d_tensor* feats, const l3d_tensor* ids,

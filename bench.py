@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
+    ap.add_argument("--workload", default="chain", choices=["chain", "vggt"],
+                    help="chain: config 5 fused layer-op chain (GB/s); vggt: config 2 "
+                         "aggregator block stack (tokens/s)")
     return ap.parse_args()
 
 
@@ -245,11 +248,127 @@ def time_cpu_chain(orc, C, rows, seed, min_seconds=10.0):
 
 
 # -------------------------------------------------------------------- main
+def vggt_inputs(dev, S=8, seed=20261201):
+    """Config 2: pixels [S, 3, 518, 518] ~ U(0,1); patch-embed weights ~ N(0, 0.02);
+    camera / register tokens (slot 0 for the first view, slot 1 for the others,
+    crate/runtime/vggt.rs:246-262)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    C, p, hw = 1024, 14, 518
+    np_ = (hw // p) ** 2
+    bf = torch.bfloat16
+    inp = {
+        "pixels": torch.rand(S, 3, hw, hw, generator=g).to(bf),
+        "w": (0.02 * torch.randn(C, 3, p, p, generator=g)).to(bf),
+        "b": (0.02 * torch.randn(C, generator=g)).to(bf),
+        "pos": (0.02 * torch.randn(1 + np_, C, generator=g)).to(bf),
+        "cls": (0.02 * torch.randn(C, generator=g)).to(bf),
+        "reg": (0.02 * torch.randn(4, C, generator=g)).to(bf),
+        "special": (0.02 * torch.randn(2, 5, C, generator=g)).to(bf),
+    }
+    return {k: v.to(dev) for k, v in inp.items()}
+
+
+def run_vggt(args, world, rank, local):
+    """Config 2 stack: patch embedding (l3d_patch_embed) of S = 8 views, the
+    camera/register tokens, then 24 frame + 24 global VGGT blocks
+    (candle-3d_b200/blocks.py).  One step = one aggregator forward; the metric
+    is tokens/s (S * 1374 tokens per step)."""
+    import torch
+
+    import __graft_entry__ as graft
+
+    pkg = graft.load_package()
+    from candle3d_b200 import blocks
+
+    ops = pkg.ops
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    S, ph = 8, 37
+    N = 5 + ph * ph
+    inp = vggt_inputs(dev, S)
+    agg = blocks.VggtAggregator(depth=24, device=dev)
+    fpos = blocks.VggtAggregator.positions(1, S, ph, ph, 5, dev)
+    gpos = fpos.reshape(1, S * N, 2)
+    special = torch.cat([inp["special"][:1], inp["special"][1:].expand(S - 1, 5, 1024)], 0)
+
+    def step(pixels):
+        tok = ops.patch_embed(pixels, inp["w"], inp["b"], inp["pos"], inp["cls"], inp["reg"], 14)
+        tokens = torch.cat([special, tok[:, 5:]], 1)
+        return agg.forward(tokens, fpos, gpos, S)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step(inp["pixels"])
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(inp["pixels"])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    tokens_step = S * N
+    value = tokens_step * args.steps / (ms / 1e3)
+    # Per frame/global block pair: linears 2 x 24 T C^2, attention 4 S N^2 C
+    # (frame) + 4 (S N)^2 C (global); 24 pairs (about 2.66e13 FLOP per step).
+    C = 1024
+    flops = 24 * (2 * 24 * tokens_step * C * C + 4 * S * N * N * C + 4 * (S * N) ** 2 * C)
+    peak_tf = 1402.3
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak_tf = float(json.loads(pk.read_text()).get("bf16_tflops_sustained", peak_tf))
+    ach = flops / (ms / args.steps / 1e3) / 1e12
+    # End to end: pixels from pinned host memory in, final tokens back out.
+    hp = inp["pixels"].cpu().pin_memory()
+    dp = torch.empty_like(inp["pixels"])
+    hy = torch.empty((S, N, 1024), dtype=torch.bfloat16).pin_memory()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n2 = max(1, min(args.steps, 5))
+    a0.record(stream)
+    for _ in range(n2):
+        dp.copy_(hp, non_blocking=True)
+        hy.copy_(step(dp), non_blocking=True)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    ems = a0.elapsed_time(a1)
+    line = {
+        "metric": "block-stack tokens/s", "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config 2 shapes)",
+        "config": {"workload": "config2 VGGT-1B aggregator: patch embed + 24 frame / 24 global "
+                               "blocks, S=8 views x 1374 tokens, dim 1024, 16 heads, MLP 4096",
+                   "parallelism": "single GPU (global attention couples all views)",
+                   "baseline_metric": BASELINE_METRIC},
+        "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + SDPA + fused ops)",
+                     "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": round(ach / peak_tf, 4), "traffic": None},
+        "clocks": clocks,
+        "e2e": {"value": round(tokens_step * n2 / (ems / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(hp.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "vggt":
+        if world > 1 or args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": args.impl, "workload": "vggt", "unavailable":
+                                  "the VGGT stack runs on one GPU (global attention couples all "
+                                  "views; K/V all-gather sharding is not built) and has no CPU arm"}))
+            return 0
+        return run_vggt(args, world, rank, local)
     C, T = args.channels, args.rows
     H, D, kind = head_cfg(C)
     workload = (f"config5 fused chain: LN+adaLN-modulate -> "

@@ -44,6 +44,20 @@ constexpr int TMEM_COLS = 512;              // two 256-column accumulators
 constexpr int N_DQ_WARPS = 8;
 constexpr int THREADS = (6 + N_DQ_WARPS) * 32;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+// Operand-B modes.  MODE_RAW_TMA / MODE_RAW_LDG decode GGML blocks in the
+// prologue (3 stages of x + B + raw window); MODE_BF16 streams a bf16 copy of
+// the decoded weights with TMA (4 stages of x + B), used when the M dimension
+// is large enough that decoding per 128-row tile would repeat the work
+// hundreds of times.
+enum { MODE_RAW_TMA = 0, MODE_RAW_LDG = 1, MODE_BF16 = 2 };
+template <int MODE>
+struct ModeCfg {
+  static constexpr bool FUSED = MODE != MODE_BF16;
+  static constexpr int NST = FUSED ? 3 : 4;
+  static constexpr int RAW = FUSED ? RAW_BYTES : 0;
+  static constexpr int SMEM = NST * (A_BYTES + B_BYTES + RAW) + 1024 + 256;
+};
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 // Status word codes written by the kernel into the workspace header.
@@ -252,17 +266,21 @@ __device__ __forceinline__ void dequant_tile(const Params& p, const uint8_t* raw
   }
 }
 
-template <bool RAW_TMA>
+template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                  const Params p) {
+  constexpr bool RAW_TMA = MODE == MODE_RAW_TMA;
+  constexpr bool FUSED = ModeCfg<MODE>::FUSED;
+  constexpr int STAGES = ModeCfg<MODE>::NST;
+  constexpr int RAWB = ModeCfg<MODE>::RAW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sa = smem;                              // [STAGES][A_BYTES]
   uint8_t* sb = smem + STAGES * A_BYTES;           // [STAGES][B_BYTES]
-  uint8_t* sr = sb + STAGES * B_BYTES;             // [STAGES][RAW_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sr + STAGES * RAW_BYTES);
+  uint8_t* sr = sb + STAGES * B_BYTES;             // [STAGES][RAWB] (fused modes)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sr + STAGES * RAWB);
   uint64_t* lfull = bars;                          // [STAGES] TMA -> dequant/MMA
   uint64_t* bfull = bars + STAGES;                 // [STAGES] dequant -> MMA
   uint64_t* empty = bars + 2 * STAGES;             // [STAGES] MMA -> producer
@@ -309,12 +327,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
-          mbar_expect_tx(&lfull[stage], RAW_TMA ? A_BYTES + RAW_BYTES : A_BYTES);
+          mbar_expect_tx(&lfull[stage], MODE == MODE_RAW_TMA ? A_BYTES + RAW_BYTES
+                                        : MODE == MODE_BF16  ? A_BYTES + B_BYTES
+                                                             : A_BYTES);
           tma_load_2d(sa + stage * A_BYTES, &map_x, &lfull[stage], kb * BK, m0);
-          if (RAW_TMA) {
+          if constexpr (RAW_TMA) {
             // 16-byte aligned window (in 2-byte elements) holding this K step.
             const int c0 = ((kb * p.bpt) >> 4) << 3;
-            tma_load_2d(sr + stage * RAW_BYTES, &map_w, &lfull[stage], c0, n0);
+            tma_load_2d(sr + stage * RAWB, &map_w, &lfull[stage], c0, n0);
+          }
+          if constexpr (MODE == MODE_BF16) {
+            tma_load_2d(sb + stage * B_BYTES, &map_w, &lfull[stage], kb * BK, n0);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -335,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW) ||
-              !mbar_wait(&bfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_FULL)) {
+              (FUSED && !mbar_wait(&bfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_FULL))) {
             ok = false;
             break;
           }
@@ -412,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
-  } else {
+  } else if constexpr (FUSED) {
     // --------------------------------------------------------- dequantisers
     const int t = threadIdx.x - 6 * 32;  // 0 .. 255
     int stage = 0;
@@ -427,7 +450,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        dequant_tile<RAW_TMA>(p, sr + stage * RAW_BYTES, sb + stage * B_BYTES, n0, kb, t);
+        dequant_tile<RAW_TMA>(p, sr + stage * RAWB, sb + stage * B_BYTES, n0, kb, t);
         // Generic-proxy smem writes must be visible to the tensor core.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -481,12 +504,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // x: bf16 [rows, cols] with row stride ld elements; box rows x 64, 128B swizzle.
 static bool make_map_x(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
-                       uint64_t ld) {
+                       uint64_t ld, uint32_t box_rows = BM) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * 2};
-  const cuuint32_t box[2] = {uint32_t(BK), uint32_t(BM)};
+  const cuuint32_t box[2] = {uint32_t(BK), box_rows};
   const cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -525,13 +548,19 @@ using namespace l3d;
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Workspace: [0, 256) status word; then a bf16 copy of the activations when x
-// is F32 or its rows are not 16-byte aligned.
+// Above this many rows the weights are decoded once per call into the
+// workspace instead of once per 128-row tile.
+constexpr int64_t kDecodeOnceRows = 512;
+
+// Workspace: [0, 256) status word; a bf16 copy of the activations (used when
+// x is F32 or its rows are not 16-byte aligned); for m > kDecodeOnceRows the
+// decoded bf16 weights [n, k].
 extern "C" size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t n, int64_t k) {
   (void)fmt;
-  (void)n;
-  if (m < 0 || k < 0) return 0;
-  return 256 + align256(size_t(m) * size_t(k) * 2);
+  if (m < 0 || k < 0 || n < 0) return 0;
+  size_t bytes = 256 + align256(size_t(m) * size_t(k) * 2);
+  if (m > kDecodeOnceRows) bytes += align256(size_t(n) * size_t(k) * 2);
+  return bytes;
 }
 
 extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n,
@@ -616,24 +645,52 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
   CUtensorMap map_x, map_w;
   if (!make_map_x(&map_x, xa, uint64_t(M), uint64_t(k), uint64_t(lda)))
     return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for x", op);
-  // The TMA window needs 16-byte aligned weight rows (k % 256 == 0).
-  const bool raw_tma = (reinterpret_cast<uintptr_t>(wq) % 16 == 0) && (p.row_bytes % 16 == 0) &&
-                       make_map_w(&map_w, wq, uint64_t(n), uint64_t(p.row_bytes));
-  if (!raw_tma) map_w = map_x;  // unused
+  int mode;
+  if (M > kDecodeOnceRows) {
+    // Decode the weights once into the workspace (bf16 [n, k]), then stream
+    // them with TMA like the activations.
+    char* wb = ws + 256 + align256(size_t(M) * size_t(k) * 2);
+    int rc = launch_dequantize(wq, fmt, n, k, L3D_BF16, wb, s);
+    if (rc) return rc;
+    if (!make_map_x(&map_w, wb, uint64_t(n), uint64_t(k), uint64_t(k), BN))
+      return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the decoded weights", op);
+    mode = MODE_BF16;
+  } else {
+    // The TMA window needs 16-byte aligned weight rows (k % 256 == 0).
+    const bool raw_tma = (reinterpret_cast<uintptr_t>(wq) % 16 == 0) && (p.row_bytes % 16 == 0) &&
+                         make_map_w(&map_w, wq, uint64_t(n), uint64_t(p.row_bytes));
+    if (!raw_tma) map_w = map_x;  // unused
+    mode = raw_tma ? MODE_RAW_TMA : MODE_RAW_LDG;
+  }
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(qgemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    SMEM_BYTES);
+    attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_RAW_TMA>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ModeCfg<MODE_RAW_TMA>::SMEM);
     if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(qgemm_kernel<false>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_RAW_LDG>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      ModeCfg<MODE_RAW_LDG>::SMEM);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_BF16>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      ModeCfg<MODE_BF16>::SMEM);
   });
   if (attr_err != cudaSuccess)
-    return fail(L3D_E_CUDA, "%s: cannot reserve %d bytes of shared memory", op, SMEM_BYTES);
+    return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
   const int tiles = int(((M + BM - 1) / BM) * ((n + BN - 1) / BN));
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  if (raw_tma) qgemm_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(map_x, map_w, p);
-  else qgemm_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(map_x, map_w, p);
+  switch (mode) {
+    case MODE_RAW_TMA:
+      qgemm_kernel<MODE_RAW_TMA><<<grid, THREADS, ModeCfg<MODE_RAW_TMA>::SMEM, s>>>(map_x, map_w, p);
+      break;
+    case MODE_RAW_LDG:
+      qgemm_kernel<MODE_RAW_LDG><<<grid, THREADS, ModeCfg<MODE_RAW_LDG>::SMEM, s>>>(map_x, map_w, p);
+      break;
+    default:
+      qgemm_kernel<MODE_BF16><<<grid, THREADS, ModeCfg<MODE_BF16>::SMEM, s>>>(map_x, map_w, p);
+      break;
+  }
   return check_launch(op);
 }

@@ -30,6 +30,7 @@ struct RowNormParams {
   int add_input;           // y += r after the gate
   int norm;                // NormKind
   float eps;
+  int nbatch;              // batches of the staged coefficients (1 = broadcast)
 };
 
 constexpr int kBlock = 256;
@@ -86,12 +87,50 @@ __device__ __forceinline__ void st_packed(T* p, const typename Packed<T, VEC>::S
   else __stcs(reinterpret_cast<uint4*>(p), s);
 }
 
+template <int VEC>
+__device__ __forceinline__ void ld_smem_vec(const float* p, float (&f)[VEC]) {
+  if constexpr (VEC % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(p + i);
+      f[i] = t.x; f[i + 1] = t.y; f[i + 2] = t.z; f[i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = p[i];
+  }
+}
+
 // RES: the residual branch is present (x and h both held in registers).
-template <typename T, int VEC, int G, int kNV, bool RES>
+// STG: the per-channel vectors are folded once per block into shared memory,
+//   A = w (1 + scale), Bc = b (1 + scale) + shift (and the output gate), so
+//   the output costs one FFMA per element instead of several vector loads.
+template <typename T, int VEC, int G, int kNV, bool RES, bool STG>
 __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
     rownorm_kernel(const RowNormParams p) {
   using S = typename Packed<T, VEC>::S;
   __shared__ float red[kBlock / 32];
+  extern __shared__ float coef[];  // STG: [nbatch, C] A, [nbatch, C] Bc, [nbatch, C] gate
+  if constexpr (STG) {
+    const int64_t nc = int64_t(p.nbatch) * p.C;
+    for (int64_t i = threadIdx.x; i < nc; i += blockDim.x) {
+      const int64_t bb = i / p.C, c = i - bb * p.C;
+      float w[1] = {1.f}, bi[1] = {0.f}, sc[1] = {0.f}, sh[1] = {0.f};
+      if (p.w.ptr) load_chan<1>(p.w, 0, c, w);
+      if (p.b.ptr) load_chan<1>(p.b, 0, c, bi);
+      if (p.scale.ptr) load_chan<1>(p.scale, bb, c, sc);
+      if (p.shift.ptr) load_chan<1>(p.shift, bb, c, sh);
+      const float s1 = 1.f + sc[0];
+      coef[i] = w[0] * s1;
+      coef[nc + i] = bi[0] * s1 + sh[0];
+      if (p.g2.ptr) {
+        float g[1];
+        load_chan<1>(p.g2, bb, c, g);
+        coef[2 * nc + i] = g[0];
+      }
+    }
+    __syncthreads();
+  }
   constexpr int RPB = kBlock / G;  // rows per block
   const int tid = threadIdx.x % G;
   const int64_t nvec = p.C / VEC;
@@ -214,6 +253,27 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
     unpack_v<T, VEC>(v[i], a);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) o[e] = (a[e] - mean) * inv;
+    if constexpr (STG) {
+      // Folded per-channel coefficients: o * A + Bc [then gate, + input].
+      const float* ca = coef + (p.nbatch > 1 ? b : 0) * p.C + c0;
+      const float* cb = ca + p.nbatch * p.C;
+      float fa[VEC], fb[VEC];
+      ld_smem_vec<VEC>(ca, fa);
+      ld_smem_vec<VEC>(cb, fb);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = o[e] * fa[e] + fb[e];
+      if (p.g2.ptr) {
+        ld_smem_vec<VEC>(cb + p.nbatch * p.C, t);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = t[e] * o[e];
+      }
+      if (p.add_input) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = o[e] + a[e];
+      }
+      st_packed<T, VEC>(yr + c0, pack_v<T, VEC>(o));
+      continue;
+    }
     if (p.w.ptr) {
       load_chan<VEC>(p.w, 0, c0, t);
 #pragma unroll
@@ -249,36 +309,44 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
 }
 
 // Resident blocks of one kernel instance on the whole device (one full wave).
-template <typename T, int VEC, int G, int NV, bool RES>
+constexpr size_t kStageMax = 48 * 1024;  // shared-memory budget of the folded coefficients
+
+template <typename T, int VEC, int G, int NV, bool RES, bool STG>
 static int64_t rownorm_wave() {
   static const int64_t wave = [] {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rownorm_kernel<T, VEC, G, NV, RES>,
-                                                      kBlock, 0) != cudaSuccess || n < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rownorm_kernel<T, VEC, G, NV, RES, STG>,
+                                                      kBlock, STG ? kStageMax : 0) != cudaSuccess ||
+        n < 1)
       n = 1;
     return int64_t(n) * sm_count();
   }();
   return wave;
 }
 
-template <typename T, int VEC, int G, int NV, bool RES>
-static void launch_rownorm_k(const RowNormParams& p, cudaStream_t s) {
+template <typename T, int VEC, int G, int NV, bool RES, bool STG>
+static void launch_rownorm_k(const RowNormParams& p, size_t smem, cudaStream_t s) {
   constexpr int rpb = kBlock / G;
   int64_t blocks = (p.rows + rpb - 1) / rpb;
   // Persistent: at most kWaves resident waves of blocks, each block striding
   // over row groups.
-  const int64_t cap = kWaves * rownorm_wave<T, VEC, G, NV, RES>();
+  const int64_t cap = kWaves * rownorm_wave<T, VEC, G, NV, RES, STG>();
   if (blocks > cap) blocks = cap;
-  rownorm_kernel<T, VEC, G, NV, RES><<<dim3(unsigned(blocks)), kBlock, 0, s>>>(p);
+  rownorm_kernel<T, VEC, G, NV, RES, STG><<<dim3(unsigned(blocks)), kBlock, smem, s>>>(p);
 }
 
 template <typename T, int VEC, int NV>
-static void launch_rownorm_g(const RowNormParams& p, int G, cudaStream_t s) {
+static void launch_rownorm_g(const RowNormParams& p, int G, size_t smem, cudaStream_t s) {
   switch (G) {
-#define L3D_CASE(GG)                                        \
-  case GG:                                                  \
-    if (p.h) launch_rownorm_k<T, VEC, GG, NV, true>(p, s);  \
-    else launch_rownorm_k<T, VEC, GG, NV, false>(p, s);     \
+#define L3D_CASE(GG)                                                          \
+  case GG:                                                                    \
+    if (p.h) {                                                                \
+      if (smem) launch_rownorm_k<T, VEC, GG, NV, true, true>(p, smem, s);     \
+      else launch_rownorm_k<T, VEC, GG, NV, true, false>(p, 0, s);            \
+    } else {                                                                  \
+      if (smem) launch_rownorm_k<T, VEC, GG, NV, false, true>(p, smem, s);    \
+      else launch_rownorm_k<T, VEC, GG, NV, false, false>(p, 0, s);           \
+    }                                                                         \
     break;
     L3D_CASE(8) L3D_CASE(16) L3D_CASE(32) L3D_CASE(64) L3D_CASE(128) L3D_CASE(256)
 #undef L3D_CASE
@@ -287,13 +355,13 @@ static void launch_rownorm_g(const RowNormParams& p, int G, cudaStream_t s) {
 }
 
 template <typename T, int VEC>
-static void launch_rownorm(const RowNormParams& p, int G, int NV, cudaStream_t s) {
+static void launch_rownorm(const RowNormParams& p, int G, int NV, size_t smem, cudaStream_t s) {
   if constexpr (VEC == 1) {
-    launch_rownorm_g<T, VEC, 16>(p, G, s);
+    launch_rownorm_g<T, VEC, 16>(p, G, smem, s);
   } else {
-    if (NV <= 2) launch_rownorm_g<T, VEC, 2>(p, G, s);
-    else if (NV <= 4) launch_rownorm_g<T, VEC, 4>(p, G, s);
-    else launch_rownorm_g<T, VEC, 8>(p, G, s);
+    if (NV <= 2) launch_rownorm_g<T, VEC, 2>(p, G, smem, s);
+    else if (NV <= 4) launch_rownorm_g<T, VEC, 4>(p, G, smem, s);
+    else launch_rownorm_g<T, VEC, 8>(p, G, smem, s);
   }
 }
 
@@ -404,9 +472,16 @@ static int run_rownorm(const RowNormArgs& a, cudaStream_t stream) {
   if (!pick_geometry(nvec, !vec_ok, &G, &NV))
     return fail(L3D_E_UNSUPPORTED, "%s: row length %lld exceeds the per-row limit", op,
                 (long long)p.C);
+  // Fold the per-channel vectors into shared memory when they fit.
+  p.nbatch = (p.scale.bstride || p.shift.bstride || p.g2.bstride) ? int(B) : 1;
+  size_t smem = 0;
+  if (p.norm != NORM_NONE) {
+    const size_t need = size_t(p.nbatch) * size_t(p.C) * sizeof(float) * (p.g2.ptr ? 3 : 2);
+    if (need <= kStageMax) smem = need;
+  }
   L3D_DISPATCH_FLOAT(a.x->dtype, T, {
-    if (vec_ok) launch_rownorm<T, Vec16<T>::N>(p, G, NV, stream);
-    else launch_rownorm<T, 1>(p, G, NV, stream);
+    if (vec_ok) launch_rownorm<T, Vec16<T>::N>(p, G, NV, smem, stream);
+    else launch_rownorm<T, 1>(p, G, NV, smem, stream);
   });
   return check_launch(op);
 }

@@ -34,16 +34,20 @@
 namespace l3d {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int RAW_ROW = 96;                 // bytes of the raw window per W row
 constexpr int A_BYTES = BM * BK * 2;        // 16 KB
 constexpr int B_BYTES = BN * BK * 2;        // 32 KB
 constexpr int RAW_BYTES = BN * RAW_ROW;     // 24 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + RAW_BYTES;
 constexpr int TMEM_COLS = 512;              // two 256-column accumulators
 constexpr int N_DQ_WARPS = 8;
 constexpr int THREADS = (6 + N_DQ_WARPS) * 32;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// Epilogue staging (decode-once mode): per epilogue warp 32 rows x 64 columns
+// in 128B-swizzled boxes of 128 bytes per row (one box of 64 bf16, or two of
+// 32 f32), written by TMA stores whole 128-byte lines at a time.
+constexpr int EPI_COLS = 64;
+constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 4;  // 8 KB
+constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
 // Operand-B modes.  MODE_RAW_TMA / MODE_RAW_LDG decode GGML blocks in the
 // prologue (3 stages of x + B + raw window); MODE_BF16 streams a bf16 copy of
@@ -56,7 +60,8 @@ struct ModeCfg {
   static constexpr bool FUSED = MODE != MODE_BF16;
   static constexpr int NST = FUSED ? 3 : 4;
   static constexpr int RAW = FUSED ? RAW_BYTES : 0;
-  static constexpr int SMEM = NST * (A_BYTES + B_BYTES + RAW) + 1024 + 256;
+  static constexpr int EPI = FUSED ? 0 : EPI_BYTES;  // fused modes store directly
+  static constexpr int SMEM = NST * (A_BYTES + B_BYTES + RAW) + EPI + 1024 + 256;
 };
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
@@ -92,6 +97,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+// As mbar_try_wait, but the thread may be suspended (up to ~1 us) until the
+// phase completes, so waiting warps do not take issue slots from the warps
+// that do the work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the warps that are not on the MMA critical path.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, int* status, int code) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait_suspend(bar, parity)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+  return true;
 }
 // Bounded wait: returns false (and raises the CTA abort flag) on timeout or
 // when another role of the CTA has already aborted.
@@ -158,6 +191,41 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// 16 consecutive f32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Tiled TMA store of a 32-row x 16-column box from shared memory, and the
+// bulk-group bookkeeping around it.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // 32 consecutive f32 accumulator columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -189,6 +257,7 @@ struct Params {
   int64_t row_bytes;
   int fmt;
   int bpt;            // raw bytes per 64-wide K step (2 blocks)
+  int tma_store;      // epilogue writes y through the map_y tensor map
 };
 
 // int8 -> f32 exactly: place (q ^ 0x80) = q + 128 in the mantissa of 2^23.
@@ -269,7 +338,7 @@ __device__ __forceinline__ void dequant_tile(const Params& p, const uint8_t* raw
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                 const Params p) {
+                 const __grid_constant__ CUtensorMap map_y, const Params p) {
   constexpr bool RAW_TMA = MODE == MODE_RAW_TMA;
   constexpr bool FUSED = ModeCfg<MODE>::FUSED;
   constexpr int STAGES = ModeCfg<MODE>::NST;
@@ -280,7 +349,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sa = smem;                              // [STAGES][A_BYTES]
   uint8_t* sb = smem + STAGES * A_BYTES;           // [STAGES][B_BYTES]
   uint8_t* sr = sb + STAGES * B_BYTES;             // [STAGES][RAWB] (fused modes)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sr + STAGES * RAWB);
+  uint8_t* se = sr + STAGES * RAWB;                // [4 warps][8 KB] epilogue staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(se + ModeCfg<MODE>::EPI);
   uint64_t* lfull = bars;                          // [STAGES] TMA -> dequant/MMA
   uint64_t* bfull = bars + STAGES;                 // [STAGES] dequant -> MMA
   uint64_t* empty = bars + 2 * STAGES;             // [STAGES] MMA -> producer
@@ -385,10 +455,82 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, ST_TIMEOUT_TMEM)) break;
+      if (!mbar_wait_idle(&tfull[acc], acc_phase, abort_flag, p.status, ST_TIMEOUT_TMEM)) break;
       tc_fence_after();
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+      if constexpr (!FUSED) if (p.tma_store) {
+        // 32 rows x 64 columns per step: TMEM -> registers (+ bias) -> this
+        // warp's staging (128B-swizzled boxes of 128 bytes per row) -> TMA
+        // stores of whole 128-byte lines; rows / columns past the matrix are
+        // clipped by the tensor map.
+        uint8_t* stg = se + (warp - 2) * EPI_WARP_BYTES;
+        const bool f32 = p.y_dtype == L3D_F32;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += EPI_COLS) {
+          float v[EPI_COLS];
+          {
+            float a[32], b[32];
+            tmem_ld32(taddr + uint32_t(c), a);
+            tmem_ld32(taddr + uint32_t(c + 32), b);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = b[i]; }
+          }
+          const int col0 = n0 + c;
+          if (col0 >= p.N) continue;  // warp-uniform
+          if (p.bias) {
+            if (col0 + EPI_COLS <= p.N && p.bias_dtype == L3D_F32) {
+              const float4* b4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col0);
+#pragma unroll
+              for (int q = 0; q < EPI_COLS / 4; ++q) {
+                const float4 t = __ldg(b4 + q);
+                v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < EPI_COLS; ++i) {
+                const int col = col0 + i < p.N ? col0 + i : p.N - 1;
+                v[i] += p.bias_dtype == L3D_F32
+                            ? __ldg(static_cast<const float*>(p.bias) + col)
+                            : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[col]);
+              }
+            }
+          }
+          // The previous stores from this staging area must have read it.
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          // Row `lane` of a box is 128 bytes = 8 chunks of 16 B; chunk j lives
+          // at chunk j ^ (lane % 8) (the SWIZZLE_128B pattern of the map).
+          uint8_t* rowp = stg + lane * 128;
+          if (f32) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {  // two boxes of 32 columns
+              const int bx = q >> 3, j = q & 7;
+              *reinterpret_cast<float4*>(rowp + bx * 4096 + ((j ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = v[8 * j + e];
+              *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = pack(f, __nv_bfloat16());
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_y, stg, col0, m0 + quarter * 32);
+            if (f32 && col0 + 32 < p.N) tma_store_2d(&map_y, stg + 4096, col0 + 32, m0 + quarter * 32);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
@@ -435,6 +577,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (p.tma_store && lane == 0) bulk_wait0();  // stores complete before teardown
   } else if constexpr (FUSED) {
     // --------------------------------------------------------- dequantisers
     const int t = threadIdx.x - 6 * 32;  // 0 .. 255
@@ -514,6 +657,23 @@ static bool make_map_x(CUtensorMap* m, const void* base, uint64_t rows, uint64_t
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Output y [rows, cols] (bf16 or f32, row stride ld elements); box 32 rows x
+// EPI_COLS columns, unswizzled, for the epilogue's TMA stores.
+static bool make_map_y(CUtensorMap* m, void* base, int dtype, uint64_t rows, uint64_t cols,
+                       uint64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const uint64_t es = dtype == L3D_F32 ? 4 : 2;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * es};
+  const cuuint32_t box[2] = {uint32_t(128 / es), 32u};  // 128-byte rows
+  const cuuint32_t el[2] = {1, 1};
+  return fn(m, dtype == L3D_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+            2, base, dims, strides, box, el, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Raw blocks viewed as uint16 [n, row_bytes / 2]; box 256 rows x 48 elements (96 B).
@@ -642,9 +802,17 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
   p.fmt = fmt;
   p.row_bytes = (k / 32) * block_bytes(fmt);
   p.bpt = 2 * block_bytes(fmt);
-  CUtensorMap map_x, map_w;
+  CUtensorMap map_x, map_w, map_y;
   if (!make_map_x(&map_x, xa, uint64_t(M), uint64_t(k), uint64_t(lda)))
     return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for x", op);
+  // TMA-store epilogue when y's base and row stride are 16-byte aligned;
+  // otherwise the epilogue stores directly.
+  const int yes = y->dtype == L3D_F32 ? 4 : 2;
+  p.tma_store = (reinterpret_cast<uintptr_t>(p.y) % 16 == 0) && ((y_ld * yes) % 16 == 0) &&
+                        make_map_y(&map_y, p.y, y->dtype, uint64_t(M), uint64_t(n), uint64_t(y_ld))
+                    ? 1
+                    : 0;
+  if (!p.tma_store) map_y = map_x;  // unused
   int mode;
   if (M > kDecodeOnceRows) {
     // Decode the weights once into the workspace (bf16 [n, k]), then stream
@@ -661,6 +829,7 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
                          make_map_w(&map_w, wq, uint64_t(n), uint64_t(p.row_bytes));
     if (!raw_tma) map_w = map_x;  // unused
     mode = raw_tma ? MODE_RAW_TMA : MODE_RAW_LDG;
+    p.tma_store = 0;  // no shared memory left for staging: direct stores
   }
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
@@ -683,13 +852,13 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
   const int grid = tiles < sm_count() ? tiles : sm_count();
   switch (mode) {
     case MODE_RAW_TMA:
-      qgemm_kernel<MODE_RAW_TMA><<<grid, THREADS, ModeCfg<MODE_RAW_TMA>::SMEM, s>>>(map_x, map_w, p);
+      qgemm_kernel<MODE_RAW_TMA><<<grid, THREADS, ModeCfg<MODE_RAW_TMA>::SMEM, s>>>(map_x, map_w, map_y, p);
       break;
     case MODE_RAW_LDG:
-      qgemm_kernel<MODE_RAW_LDG><<<grid, THREADS, ModeCfg<MODE_RAW_LDG>::SMEM, s>>>(map_x, map_w, p);
+      qgemm_kernel<MODE_RAW_LDG><<<grid, THREADS, ModeCfg<MODE_RAW_LDG>::SMEM, s>>>(map_x, map_w, map_y, p);
       break;
     default:
-      qgemm_kernel<MODE_BF16><<<grid, THREADS, ModeCfg<MODE_BF16>::SMEM, s>>>(map_x, map_w, p);
+      qgemm_kernel<MODE_BF16><<<grid, THREADS, ModeCfg<MODE_BF16>::SMEM, s>>>(map_x, map_w, map_y, p);
       break;
   }
   return check_launch(op);

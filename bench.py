@@ -49,9 +49,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
-    ap.add_argument("--workload", default="chain", choices=["chain", "vggt"],
-                    help="chain: config 5 fused layer-op chain (GB/s); vggt: config 2 "
-                         "aggregator block stack (tokens/s)")
+    ap.add_argument("--workload", default="chain", choices=["chain", "vggt", "triposg", "trellis"],
+                    help="chain: config 5 fused layer-op chain (GB/s); vggt / triposg / "
+                         "trellis: config 2 / 3 / 4 block stacks (tokens/s)")
     return ap.parse_args()
 
 
@@ -356,19 +356,102 @@ def run_vggt(args, world, rank, local):
     return 0
 
 
+def run_dit(args, local):
+    """Config 3 (TripoSG DiT: CFG batch 2 x (2048 latents + timestep token),
+    21 blocks, width 2048, cross attention to 1370 x 1024 tokens) or config 4
+    (TRELLIS.2 SLAT: ~31.5k voxels from Bernoulli(0.12) on 64^3, width 1536,
+    24 blocks, Q8_0 weights through the dequant-linear, cond 1029 x 1024).
+    One step = one model forward; the metric is tokens/s."""
+    import torch
+
+    import __graft_entry__ as graft
+
+    graft.load_package()
+    from candle3d_b200 import blocks
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(20261201)
+    bf = torch.bfloat16
+    if args.workload == "triposg":
+        model = blocks.TripoSgDit(device=dev)
+        lat = torch.randn(2, 2048, 64, generator=g).to(dev, bf)
+        cond = torch.randn(2, 1370, 1024, generator=g).to(dev, bf)
+        cond[0].zero_()  # CFG batch [uncond (zeros), cond]
+        t = torch.tensor([1000.0 * float(torch.rand(1, generator=g))], device=dev)
+        host_in = lat
+        step = lambda xin: model.forward(xin, t, cond)  # noqa: E731
+        tokens = 2 * 2049
+        desc = ("config3 TripoSG DiT: CFG batch 2 x 2049 tokens, 21 blocks, width 2048, 16 heads, "
+                "FFN 8192 GELU-erf, cross attention to 1370 x 1024")
+    else:
+        model = blocks.Trellis2Slat(device=dev)
+        occ = torch.rand(64, 64, 64, generator=g) < 0.12
+        coords = torch.nonzero(occ).to(torch.int32).to(dev)
+        feats = torch.randn(coords.shape[0], 32, generator=g).to(dev, bf)
+        cond = torch.randn(1, 1029, 1024, generator=g).to(dev, bf)
+        t = torch.tensor([1000.0 * float(torch.rand(1, generator=g))], device=dev)
+        host_in = feats
+        step = lambda xin: model.forward(xin, coords, t, cond)  # noqa: E731
+        tokens = int(coords.shape[0])
+        desc = (f"config4 TRELLIS.2 SLAT: {tokens} voxels (Bernoulli 0.12 on 64^3), 24 blocks, "
+                "width 1536, 12 heads, MLP 8192 GELU-tanh, Q8_0 dequant-linear, cond 1029 x 1024")
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step(host_in)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = step(host_in)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    hp = host_in.cpu().pin_memory()
+    dp = torch.empty_like(host_in)
+    hy = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    n2 = max(1, min(args.steps, 5))
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(n2):
+        dp.copy_(hp, non_blocking=True)
+        hy.copy_(step(dp), non_blocking=True)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    ems = a0.elapsed_time(a1)
+    line = {
+        "metric": "block-stack tokens/s", "value": round(tokens * args.steps / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": desc, "parallelism": "single GPU", "baseline_metric": BASELINE_METRIC},
+        "clocks": clocks,
+        "e2e": {"value": round(tokens * n2 / (ems / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(hp.numel() * hp.element_size()),
+                "d2h_bytes_per_step": int(hy.numel() * hy.element_size())},
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.workload == "vggt":
+    if args.workload != "chain":
         if world > 1 or args.impl == "reference":
             if rank == 0:
-                print(json.dumps({"impl": args.impl, "workload": "vggt", "unavailable":
-                                  "the VGGT stack runs on one GPU (global attention couples all "
-                                  "views; K/V all-gather sharding is not built) and has no CPU arm"}))
+                print(json.dumps({"impl": args.impl, "workload": args.workload, "unavailable":
+                                  "the block stacks run on one GPU (attention couples all tokens; "
+                                  "K/V all-gather sharding is not built) and have no CPU arm"}))
             return 0
-        return run_vggt(args, world, rank, local)
+        if args.workload == "vggt":
+            return run_vggt(args, world, rank, local)
+        return run_dit(args, local)
     C, T = args.channels, args.rows
     H, D, kind = head_cfg(C)
     workload = (f"config5 fused chain: LN+adaLN-modulate -> "

@@ -17,17 +17,24 @@ __device__ __forceinline__ float half_bits_to_f(uint16_t h) {
 // Decode one 32-weight block into f32 (unaligned byte source: blocks are 34 /
 // 18 bytes, so only 2-byte alignment is guaranteed).
 __device__ __forceinline__ void decode_block(const uint8_t* blk, int fmt, float (&w)[32]) {
-  const uint16_t dbits = uint16_t(blk[0]) | (uint16_t(blk[1]) << 8);
-  const float d = half_bits_to_f(dbits);
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(blk);  // 2-byte aligned
+  const float d = half_bits_to_f(__ldg(h));
   if (fmt == L3D_Q8_0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) w[j] = d * float(int8_t(blk[2 + j]));
+    for (int j = 0; j < 16; ++j) {
+      const uint16_t v = __ldg(h + 1 + j);
+      w[2 * j] = d * float(int8_t(v & 0xff));
+      w[2 * j + 1] = d * float(int8_t(v >> 8));
+    }
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint8_t q = blk[2 + j];
-      w[j] = d * float(int(q & 15) - 8);
-      w[16 + j] = d * float(int(q >> 4) - 8);
+    for (int j = 0; j < 8; ++j) {
+      const uint16_t v = __ldg(h + 1 + j);
+      const uint8_t q0 = v & 0xff, q1 = v >> 8;
+      w[2 * j] = d * float(int(q0 & 15) - 8);
+      w[2 * j + 1] = d * float(int(q1 & 15) - 8);
+      w[16 + 2 * j] = d * float(int(q0 >> 4) - 8);
+      w[16 + 2 * j + 1] = d * float(int(q1 >> 4) - 8);
     }
   }
 }
@@ -42,9 +49,17 @@ __global__ void dequantize_kernel(const uint8_t* __restrict__ wq, int fmt, int64
        b += int64_t(gridDim.x) * blockDim.x) {
     float w[32];
     decode_block(wq + b * bb, fmt, w);
-    TO* o = out + b * 32;  // row-major [n, k]: block b covers row b / kb, cols (b % kb) * 32
+    // Row-major [n, k]: block b is the 32 consecutive elements at b * 32,
+    // written as 16-byte vectors (the output is 16-byte aligned).
+    TO* o = out + b * 32;
+    constexpr int V = Vec16<TO>::N;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) o[j] = from_f<TO>(w[j]);
+    for (int j = 0; j < 32; j += V) {
+      float f[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) f[e] = w[j + e];
+      *reinterpret_cast<uint4*>(o + j) = pack(f, TO());
+    }
   }
 }
 
@@ -77,6 +92,8 @@ extern "C" int l3d_dequantize(const void* wq, int fmt, int64_t n, int64_t k,
   if ((k > 1 && out->strides[1] != 1) || (n > 1 && out->strides[0] != k))
     return fail(L3D_E_ALIGN, "%s: out must be contiguous", op);
   if (reinterpret_cast<uintptr_t>(wq) % 2) return fail(L3D_E_ALIGN, "%s: wq must be 2-byte aligned", op);
+  if (reinterpret_cast<uintptr_t>(elem_ptr(out)) % 16)
+    return fail(L3D_E_ALIGN, "%s: out must be 16-byte aligned", op);
   return launch_dequantize(wq, fmt, n, k, out->dtype,
                            const_cast<char*>(elem_ptr(out)), reinterpret_cast<cudaStream_t>(stream));
 }

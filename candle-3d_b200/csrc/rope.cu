@@ -26,6 +26,15 @@ __device__ __forceinline__ float inv_freq_f32(float theta, float num, float den)
   return __fdiv_rn(1.0f, p);
 }
 
+// sin / cos of an exactly formed angle: the accurate libm form for f32
+// activations; the hardware approximation for 16-bit activations (absolute
+// error about 1e-5 at |angle| <= 64, far below half an ulp of bf16 / f16).
+template <typename T>
+__device__ __forceinline__ void sincos_t(float a, float* s, float* c) {
+  if constexpr (sizeof(T) == 2) __sincosf(a, s, c);
+  else sincosf(a, s, c);
+}
+
 __device__ __forceinline__ float load_index_f(const void* p, int dtype, int64_t off) {
   if (dtype == L3D_I64) return static_cast<float>(static_cast<const int64_t*>(p)[off]);
   if (dtype == L3D_U32) return static_cast<float>(static_cast<const uint32_t*>(p)[off]);
@@ -127,7 +136,7 @@ __global__ void __launch_bounds__(256) rope2d_kernel(const Rope2dParams p) {
       const float pos = load_index_f(p.pos, p.pos_dtype,
                                      p.pbase + b * p.psb + n * p.psn + (lane >> 4) * p.psc);
       float sv, cv;
-      sincosf(__fmul_rn(pos, invf), &sv, &cv);
+      sincos_t<T>(__fmul_rn(pos, invf), &sv, &cv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         c[i] = __shfl_sync(0xffffffffu, cv, src0 + i);
@@ -330,7 +339,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2) rope3d_kernel(con
         if (lane_on && axis[k] >= 0) {
           const float cv = load_index_f(p.coords, p.coord_dtype,
                                         p.cbase + l * p.csl + axis[k] * p.csa);
-          sincosf(__fmul_rn(cv, fr[k]), &sn[k], &cs[k]);
+          sincos_t<T>(__fmul_rn(cv, fr[k]), &sn[k], &cs[k]);
         } else {
           cs[k] = 1.f;
           sn[k] = 0.f;
@@ -370,7 +379,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2) rope3d_kernel(con
           for (int i = 0; i < EPL; ++i) ss += v[i] * v[i];
 #pragma unroll
           for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-          const float rn = 1.f / fminf(fmaxf(sqrtf(ss), 1e-12f), 1e30f);
+          // 1 / clamp(||x||, 1e-12, 1e30) = rsqrt(clamp(||x||^2, 1e-24, 1e60)).
+          const float rn = rsqrtf(fminf(fmaxf(ss, 1e-24f), 1e30f * 1e30f));
           if (valid) {
             const float* g = gsm + h * p.D + m * EPL;
             float gv[EPL];

@@ -49,9 +49,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
-    ap.add_argument("--workload", default="chain", choices=["chain", "vggt", "triposg", "trellis"],
+    ap.add_argument("--workload", default="chain",
+                    choices=["chain", "vggt", "triposg", "trellis", "qlinear"],
                     help="chain: config 5 fused layer-op chain (GB/s); vggt / triposg / "
-                         "trellis: config 2 / 3 / 4 block stacks (tokens/s)")
+                         "trellis: config 2 / 3 / 4 block stacks (tokens/s); qlinear: the four "
+                         "Q8_0 linears of one config-4 block (TFLOP/s)")
     return ap.parse_args()
 
 
@@ -356,6 +358,66 @@ def run_vggt(args, world, rank, local):
     return 0
 
 
+def run_qlinear(args, local):
+    """The dequant-linear alone: one step = to_qkv (4608 x 1536), to_out
+    (1536 x 1536), mlp.0 (8192 x 1536) and mlp.2 (1536 x 8192) of one TRELLIS.2
+    block on M = 31,500 token rows, GGML Q8_0 weights (int8 per-row scales
+    ~ U(0.001, 0.02)), bf16 activations and outputs, f32 bias."""
+    import torch
+
+    import __graft_entry__ as graft
+
+    graft.load_package()
+    from candle3d_b200 import blocks
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(20261201)
+    M = 31500
+    shapes = [(4608, 1536), (1536, 1536), (8192, 1536), (1536, 8192)]
+    mms = [blocks._q8_linear(g, n, k, dev) for n, k in shapes]
+    xs = {k: torch.randn(M, k, generator=g).to(dev, torch.bfloat16) for k in {1536, 8192}}
+    flops = sum(2.0 * M * n * k for n, k in shapes)
+
+    def step():
+        for (n, k), mm in zip(shapes, mms):
+            mm(xs[k])
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    tf = flops * args.steps / (ms / 1e3) / 1e12
+    peak = 1641.7
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak = float(json.loads(pk.read_text()).get("bf16_tflops", peak))
+    print(json.dumps({
+        "metric": "dequant-linear TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (Q8_0 weights)", "data": "synthetic (seeded)",
+        "config": {"workload": "config4 block linears: M=31500 x (4608x1536, 1536x1536, "
+                               "8192x1536, 1536x8192), Q8_0", "baseline_metric": BASELINE_METRIC},
+        "roofline": {"bound": "tensor", "kernel": "qgemm_kernel (decode included)",
+                     "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tf / peak, 4), "traffic": None},
+        "gpu_launches": 2 * 4 * args.steps,
+        "clocks": clocks,
+    }))
+    return 0
+
+
 def run_dit(args, local):
     """Config 3 (TripoSG DiT: CFG batch 2 x (2048 latents + timestep token),
     21 blocks, width 2048, cross attention to 1370 x 1024 tokens) or config 4
@@ -451,6 +513,8 @@ def main():
             return 0
         if args.workload == "vggt":
             return run_vggt(args, world, rank, local)
+        if args.workload == "qlinear":
+            return run_qlinear(args, local)
         return run_dit(args, local)
     C, T = args.channels, args.rows
     H, D, kind = head_cfg(C)

@@ -527,7 +527,7 @@ def main():
             return 0
         from oracle import oracle as orc
 
-        orc.lib()
+        orc.use_all_host_threads()
         rows = args.cpu_sample_rows
         gbs, n, el = None, 0, 0.0
         vals = []
@@ -685,7 +685,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle as orc
 
-        orc.lib()
+        orc.use_all_host_threads()
         gbs, n, el = time_cpu_chain(orc, C, args.cpu_sample_rows, 7, min_seconds=10.0)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": orc.num_threads(), "kind": "port",
                "sample": f"{n} passes of {args.cpu_sample_rows} rows x C={C} ({el:.1f} s), C oracle"}

@@ -60,6 +60,16 @@ int orc_num_threads(void) {
 #endif
 }
 
+/* Use n host threads (launchers such as torchrun default OMP_NUM_THREADS to 1). */
+int orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+  return 0;
+}
+
 /* ------------------------------------------------------ LayerNorm family */
 /* Composed LayerNorm over one row, as layer_norm_no_affine
  * (crate/runtime/trellis2_blocks.rs:280-286): mean_keepdim, broadcast_sub,

@@ -55,6 +55,7 @@ def lib():
         sig = {
             "orc_round_array": [_f32p, _i64, _int],
             "orc_num_threads": [],
+            "orc_set_num_threads": [_int],
             "orc_layer_norm": [_f32p, _i64, _i64, C.c_void_p, C.c_void_p, _flt, _f32p, _int],
             "orc_layer_norm_modulate": [_f32p, _i64, _i64, _i64, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p, C.c_void_p, _int, _flt, _f32p,
@@ -106,6 +107,13 @@ def _chk(rc, name):
 
 def num_threads() -> int:
     return lib().orc_num_threads()
+
+
+def use_all_host_threads() -> int:
+    """Run the oracle on every core this process may use; returns the count."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    lib().orc_set_num_threads(n)
+    return num_threads()
 
 
 # ----------------------------------------------------------------- rounding

@@ -76,8 +76,12 @@ class VggtAggregator:
         B, N, C = y.shape
         H, D = self.H, self.D
         qkv = F.linear(y, p["qkv_w"], p["qkv_b"]).view(B, N, 3, H, D).permute(2, 0, 3, 1, 4)
+        # q / k written token-major ([B, N, H, D] memory seen as [B, H, N, D]),
+        # the layout the attention kernel keeps for its output, so the
+        # output's transpose-reshape below is a view, not a copy.
+        qk = torch.empty(2, B, N, H, D, dtype=y.dtype, device=y.device).permute(0, 1, 3, 2, 4)
         q, k = ops.qk_layernorm_rope2d(qkv[0], qkv[1], p["qnw"], p["qnb"], p["knw"], p["knb"],
-                                       1e-5, pos, 100.0)
+                                       1e-5, pos, 100.0, q_out=qk[0], k_out=qk[1])
         a = F.scaled_dot_product_attention(q, k, qkv[2])
         return F.linear(a.transpose(1, 2).reshape(B, N, C), p["proj_w"], p["proj_b"])
 

@@ -6,6 +6,8 @@
 //    optionally k) with 8 lanes per head, so the 32 distinct (half, frequency)
 //    angles of a token are formed once (one sincosf per lane) and shuffled to
 //    the lanes that need them; no cos/sin table is read in positions mode.
+//    Each lane holds both rotate-half partners, so the rotation is local, and
+//    the LayerNorm affine is folded into the rotation coefficients.
 //  * rope3d: TRELLIS.2 MultiHeadRMSNorm (x / ||x|| * gamma * sqrt(D)) + 3D RoPE
 //    over interleaved (re, im) pairs with angles coord[axis] * freq[i].  One
 //    warp owns one token; each lane keeps the angles of its own pairs for all
@@ -15,6 +17,8 @@
 // frequencies 1 / theta^(e) with e an f32 quotient, the power evaluated in
 // double and rounded once (the correctly rounded f32 result), and the angle a
 // single f32 product of the integer position and the frequency.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace l3d {
@@ -94,53 +98,152 @@ struct Rope2dParams {
   float theta;
 };
 
+// 4 consecutive elements kept packed in registers (8 bytes for 16-bit types,
+// 16 for f32) until they are used.
 template <typename T>
-__global__ void __launch_bounds__(256) rope2d_kernel(const Rope2dParams p) {
+struct Raw4 {
+  using type = typename std::conditional<sizeof(T) == 4, float4, uint2>::type;
+};
+template <typename T>
+__device__ __forceinline__ typename Raw4<T>::type load_raw4(const T* p) {
+  return __ldcs(reinterpret_cast<const typename Raw4<T>::type*>(p));
+}
+// Packed f32x2 arithmetic (FFMA2 / FADD2 / FMUL2 on sm_100): two
+// independent IEEE round-to-nearest operations per instruction.
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 as_f2(const float (&f)[4], int pr) {
+  return make_float2(f[2 * pr], f[2 * pr + 1]);
+}
+
+// Rotation coefficients of one tensor for this lane's chunks A and B with the
+// LayerNorm affine folded in.  With cos c and sin s of the chunk's four
+// frequencies, rotate_half gives
+//   out_A = (n_A w_A + b_A) c - (n_B w_B + b_B) s = n_A k1a + n_B k2a + k0a
+//   out_B = (n_B w_B + b_B) c + (n_A w_A + b_A) s = n_B k1b + n_A k2b + k0b
+// for normalised inputs n (w = 1, b = 0 without the norm).
+struct Rope2dCoef {
+  float2 k1a[2], k2a[2], k0a[2], k1b[2], k2b[2], k0b[2];
+};
+__device__ __forceinline__ void rope2d_coef(const float (*aff)[64], int ea, const float (&c)[4],
+                                            const float (&sn)[4], Rope2dCoef& k) {
+  const float4 wa4 = *reinterpret_cast<const float4*>(&aff[0][ea]);
+  const float4 wb4 = *reinterpret_cast<const float4*>(&aff[0][ea + 16]);
+  const float4 ba4 = *reinterpret_cast<const float4*>(&aff[1][ea]);
+  const float4 bb4 = *reinterpret_cast<const float4*>(&aff[1][ea + 16]);
+#pragma unroll
+  for (int pr = 0; pr < 2; ++pr) {
+    const float2 wa = pr ? make_float2(wa4.z, wa4.w) : make_float2(wa4.x, wa4.y);
+    const float2 wb = pr ? make_float2(wb4.z, wb4.w) : make_float2(wb4.x, wb4.y);
+    const float2 ba = pr ? make_float2(ba4.z, ba4.w) : make_float2(ba4.x, ba4.y);
+    const float2 bb = pr ? make_float2(bb4.z, bb4.w) : make_float2(bb4.x, bb4.y);
+    const float2 cc = as_f2(c, pr), ss = as_f2(sn, pr);
+    const float2 ns = make_float2(-ss.x, -ss.y);
+    k.k1a[pr] = __fmul2_rn(wa, cc);
+    k.k2a[pr] = __fmul2_rn(wb, ns);
+    k.k0a[pr] = __ffma2_rn(ba, cc, __fmul2_rn(bb, ns));
+    k.k1b[pr] = __fmul2_rn(wb, cc);
+    k.k2b[pr] = __fmul2_rn(wa, ss);
+    k.k0b[pr] = __ffma2_rn(bb, cc, __fmul2_rn(ba, ss));
+  }
+}
+
+// 4 packed elements -> two f32 pairs.
+template <typename T>
+__device__ __forceinline__ void unpack4x2(const typename Raw4<T>::type& u, float2 (&v)[2]) {
+  if constexpr (sizeof(T) == 4) {
+    v[0] = make_float2(u.x, u.y);
+    v[1] = make_float2(u.z, u.w);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    v[0] = make_float2(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u));
+    v[1] = make_float2(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+  } else {
+    v[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    v[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store4x2(T* p, const float2 (&v)[2]) {
+  if constexpr (sizeof(T) == 4) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+  } else {
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[i].x, v[i].y);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[i].x, v[i].y);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    __stcs(reinterpret_cast<uint2*>(p), make_uint2(w[0], w[1]));
+  }
+}
+
+// One warp per token; 8 lanes per 64-wide head row, 4 heads per iteration.
+// Lane j (0..7) of a head owns the two quarter-chunks that rotate into each
+// other: elements A = 32h + 4k + t and B = A + 16 (h = j / 4, k = j % 4,
+// t = 0..3), so rotate_half needs no data exchange.  Its four angles
+// (half h, frequency 4k + t) are formed by lanes 4j + t of the warp (lane L
+// forms half L / 16, frequency L % 16) and fetched with one shuffle each.
+// The per-head LayerNorm reduces over the head's 8 lanes (xor shuffles 1, 2,
+// 4; two passes: mean, then the centred sum of squares).  Element arithmetic
+// is packed f32x2.  Launched with 256 threads per block; 16-bit variants are
+// held to 4 blocks per SM (a few registers spill), which measured faster than
+// 3 blocks without spills.
+template <typename T>
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope2d_kernel(const Rope2dParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  const int m = lane & 7;    // element chunk [8m, 8m + 8) of a 64-wide head row
-  const int hg = lane >> 3;  // head slot within an iteration of 4 heads
+  const int j = lane & 7;     // lane within the head row
+  const int hg = lane >> 3;   // head slot within an iteration of 4 heads
+  const int ea = 32 * (j >> 2) + 4 * (j & 3);  // first element of chunk A (B = ea + 16)
   const int64_t tokens = p.B * p.N;
 
   // Lane `lane` forms the angle of (half = lane / 16, freq = lane % 16):
   // inv_freq[f] = 1 / theta^(2f / 32), Rope2d::cos_sin with dim = 32.
   const float invf = inv_freq_f32(p.theta, float(2 * (lane & 15)), 32.0f);
-  // Element e = 8m + i reads the angle (m / 4) * 16 + 8 (m % 2) + i; the sign
-  // folds rotate_half into sin_alt (negative in the first quarter of a half).
-  const int src0 = (m >> 2) * 16 + 8 * (m & 1);
-  const float sgn = (m & 3) < 2 ? -1.f : 1.f;
 
-  // LayerNorm affine of this lane's chunk, per tensor.
-  float wv[2][8], bv[2][8];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) { wv[t][i] = 1.f; bv[t][i] = 0.f; }
-    if (t < p.ntensor) {
-      if (p.w[t].ptr) load_chan<8>(p.w[t], 0, 8 * m, wv[t]);
-      if (p.b[t].ptr) load_chan<8>(p.b[t], 0, 8 * m, bv[t]);
+  // LayerNorm affine per tensor, staged in shared memory as [tensor][w|b][64]
+  // (absent weight = 1, absent bias = 0; without the norm, 1 and 0).
+  __shared__ __align__(16) float aff[2][2][64];
+  {
+    const int t = threadIdx.x >> 7, wb = (threadIdx.x >> 6) & 1, e = threadIdx.x & 63;
+    float v = wb ? 0.f : 1.f;
+    if (t < p.ntensor && p.do_norm) {
+      const ChanVec& cv = wb ? p.b[t] : p.w[t];
+      if (cv.ptr) {
+        float one[1];
+        load_chan<1>(cv, 0, e, one);
+        v = one[0];
+      }
     }
+    aff[t][wb][e] = v;
   }
+  __syncthreads();
 
   for (int64_t tok = warp0; tok < tokens; tok += nwarps) {
     const int64_t b = tok / p.N;
     const int64_t n = tok - b * p.N;
-    float c[8], s[8];
+    // cos c and sin s of this lane's four frequencies.
+    float c[4], sn[4];
     if (p.use_table) {
-      const float* cp = p.cosp + p.cbase + b * p.csb + n * p.csn + 8 * m;
-      const float* sp = p.sinp + p.sbase + b * p.ssb + n * p.ssn + 8 * m;
+      // cos_full / sin_alt_full: chunk A holds cos and -sin.
+      const float* cp = p.cosp + p.cbase + b * p.csb + n * p.csn + ea;
+      const float* sp = p.sinp + p.sbase + b * p.ssb + n * p.ssn + ea;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) { c[i] = __ldg(cp + i); s[i] = __ldg(sp + i); }
+      for (int i = 0; i < 4; ++i) { c[i] = __ldg(cp + i); sn[i] = -__ldg(sp + i); }
     } else {
       const float pos = load_index_f(p.pos, p.pos_dtype,
                                      p.pbase + b * p.psb + n * p.psn + (lane >> 4) * p.psc);
       float sv, cv;
       sincos_t<T>(__fmul_rn(pos, invf), &sv, &cv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        c[i] = __shfl_sync(0xffffffffu, cv, src0 + i);
-        s[i] = sgn * __shfl_sync(0xffffffffu, sv, src0 + i);
+      for (int i = 0; i < 4; ++i) {
+        c[i] = __shfl_sync(0xffffffffu, cv, 4 * j + i);
+        sn[i] = __shfl_sync(0xffffffffu, sv, 4 * j + i);
       }
     }
 #pragma unroll
@@ -148,61 +251,73 @@ __global__ void __launch_bounds__(256) rope2d_kernel(const Rope2dParams p) {
       if (t >= p.ntensor) break;
       const HeadView& iv = p.in[t];
       const HeadView& ov = p.out[t];
+      const T* src0 = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + n * iv.sn + ea;
+      T* dst0 = static_cast<T*>(ov.data) + ov.base + b * ov.sb + n * ov.sn + ea;
+      Rope2dCoef k;
+      rope2d_coef(aff[t], ea, c, sn, k);
       // Heads in groups of 4 iterations x 4 heads: the group's loads are all
       // issued before any arithmetic.
       constexpr int MAXIT = 4;
       for (int hb = 0; hb < p.H; hb += 4 * MAXIT) {
-      float yy[MAXIT][8];
+        typename Raw4<T>::type ra[MAXIT], rb[MAXIT];
 #pragma unroll
-      for (int it = 0; it < MAXIT; ++it) {
-        const int h = hb + it * 4 + hg;
-        if (h < p.H) {
-          const T* src = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + h * iv.sh +
-                         n * iv.sn + 8 * m;
-          load8<T>(src, yy[it]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) yy[it][i] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int it = 0; it < MAXIT; ++it) {
-        if (hb + it * 4 >= p.H) break;  // warp-uniform
-        const int h = hb + it * 4 + hg;
-        const bool valid = h < p.H;
-        float* y = yy[it];
-        if (p.do_norm) {
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) sum += y[i];
-          sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-          sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-          sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-          const float mean = sum * (1.0f / 64.0f);
-          float ss = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            y[i] -= mean;
-            ss += y[i] * y[i];
+        for (int it = 0; it < MAXIT; ++it) {
+          const int h = hb + it * 4 + hg;
+          if (h < p.H) {
+            const T* src = src0 + int64_t(h) * iv.sh;
+            ra[it] = load_raw4<T>(src);
+            rb[it] = load_raw4<T>(src + 16);
+          } else {
+            ra[it] = rb[it] = {};
           }
-          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-          const float inv = 1.f / sqrtf(ss * (1.0f / 64.0f) + p.eps);
+        }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = y[i] * inv * wv[t][i] + bv[t][i];
-        }
-        float o[8];
+        for (int it = 0; it < MAXIT; ++it) {
+          if (hb + it * 4 >= p.H) break;  // warp-uniform
+          const int h = hb + it * 4 + hg;
+          float2 a[2], bv[2];
+          unpack4x2<T>(ra[it], a);
+          unpack4x2<T>(rb[it], bv);
+          if (p.do_norm) {
+            const float2 s2 = __fadd2_rn(__fadd2_rn(a[0], a[1]), __fadd2_rn(bv[0], bv[1]));
+            float sum = s2.x + s2.y;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            const float2 nm = f2(-sum * (1.0f / 64.0f));
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float partner = __shfl_xor_sync(0xffffffffu, y[i], 2);
-          o[i] = y[i] * c[i] + partner * s[i];
+            for (int pr = 0; pr < 2; ++pr) {
+              a[pr] = __fadd2_rn(a[pr], nm);
+              bv[pr] = __fadd2_rn(bv[pr], nm);
+            }
+            float2 q2 = __fmul2_rn(a[0], a[0]);
+            q2 = __ffma2_rn(a[1], a[1], q2);
+            q2 = __ffma2_rn(bv[0], bv[0], q2);
+            q2 = __ffma2_rn(bv[1], bv[1], q2);
+            float ss = q2.x + q2.y;
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+            const float var = ss * (1.0f / 64.0f) + p.eps;
+            const float2 inv = f2(sizeof(T) == 2 ? rsqrtf(var) : 1.f / sqrtf(var));
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+              a[pr] = __fmul2_rn(a[pr], inv);
+              bv[pr] = __fmul2_rn(bv[pr], inv);
+            }
+          }
+          float2 oa[2], ob[2];
+#pragma unroll
+          for (int pr = 0; pr < 2; ++pr) {
+            oa[pr] = __ffma2_rn(a[pr], k.k1a[pr], __ffma2_rn(bv[pr], k.k2a[pr], k.k0a[pr]));
+            ob[pr] = __ffma2_rn(bv[pr], k.k1b[pr], __ffma2_rn(a[pr], k.k2b[pr], k.k0b[pr]));
+          }
+          if (h < p.H) {
+            T* dst = dst0 + int64_t(h) * ov.sh;
+            store4x2<T>(dst, oa);
+            store4x2<T>(dst + 16, ob);
+          }
         }
-        if (valid) {
-          T* dst = static_cast<T*>(ov.data) + ov.base + b * ov.sb + h * ov.sh + n * ov.sn + 8 * m;
-          store8<T>(dst, o);
-        }
-      }
       }
     }
   }

@@ -59,8 +59,10 @@ def test_layernorm_rope2d_tables(ops, orc, dev, dt, cfg, norm):
 
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
 @pytest.mark.parametrize("cfg", [(2, 16, 64, 64), (1, 16, 37, 37 * 8), (3, 5, 4, 6)])
-def test_qk_layernorm_rope2d_positions(ops, orc, dev, dt, cfg):
-    """q and k in one launch, angles from integer positions (no tables)."""
+@pytest.mark.parametrize("out_layout", ["bhnd", "bnhd"])
+def test_qk_layernorm_rope2d_positions(ops, orc, dev, dt, cfg, out_layout):
+    """q and k in one launch, angles from integer positions (no tables);
+    outputs contiguous [B, H, N, D] or token-major [B, N, H, D] memory."""
     import torch
 
     B, H, ph, pw = cfg
@@ -74,8 +76,12 @@ def test_qk_layernorm_rope2d_positions(ops, orc, dev, dt, cfg):
     bq, bqv = to_dev(0.1 * r.standard_normal(D), dt, dev)
     wk, wkv = to_dev(1 + 0.1 * r.standard_normal(D), dt, dev)
     bk, bkv = to_dev(0.1 * r.standard_normal(D), dt, dev)
+    outs = {}
+    if out_layout == "bnhd":
+        qk = torch.empty(2, B, N, H, D, dtype=qkv.dtype, device=dev).permute(0, 1, 3, 2, 4)
+        outs = {"q_out": qk[0], "k_out": qk[1]}
     qo, ko = ops.qk_layernorm_rope2d(v[0], v[1], wq, bq, wk, bk, 1e-5,
-                                     torch.from_numpy(pos).to(dev), 100.0)
+                                     torch.from_numpy(pos).to(dev), 100.0, **outs)
     cs, sn = orc.rope2d_tables(pos, 100.0, D)
     vv = qkvv.transpose(2, 0, 3, 1, 4)
     assert_close(qo.float().cpu().numpy(),

@@ -140,6 +140,64 @@ __device__ __forceinline__ uint4 pack(const float (&f)[8], __half) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Packed f32x2 arithmetic (FADD2 / FMUL2 / FFMA2 on sm_100): two independent
+// IEEE round-to-nearest operations per instruction, so element-wise work in
+// the HBM-bound kernels costs half the issue slots.
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// A 16-byte pack as float pairs (2 pairs of f32, or 4 pairs of 16-bit).
+__device__ __forceinline__ void unpack2(const uint4& u, float2 (&f)[2], float) {
+  f[0] = make_float2(__uint_as_float(u.x), __uint_as_float(u.y));
+  f[1] = make_float2(__uint_as_float(u.z), __uint_as_float(u.w));
+}
+__device__ __forceinline__ void unpack2(const uint4& u, float2 (&f)[4], __nv_bfloat16) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    f[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+}
+__device__ __forceinline__ void unpack2(const uint4& u, float2 (&f)[4], __half) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+}
+__device__ __forceinline__ uint4 pack2(const float2 (&f)[2], float) {
+  return make_uint4(__float_as_uint(f[0].x), __float_as_uint(f[0].y), __float_as_uint(f[1].x),
+                    __float_as_uint(f[1].y));
+}
+__device__ __forceinline__ uint4 pack2(const float2 (&f)[4], __nv_bfloat16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __float22bfloat162_rn(f[i]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ uint4 pack2(const float2 (&f)[4], __half) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __float22half2_rn(f[i]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+// P consecutive float pairs of an f32 array in shared or global memory
+// (16-byte aligned).
+template <int P>
+__device__ __forceinline__ void ld_pairs(const float* p, float2 (&f)[P]) {
+#pragma unroll
+  for (int i = 0; i < P; i += 2) {
+    const float4 t = *reinterpret_cast<const float4*>(p + 2 * i);
+    f[i] = make_float2(t.x, t.y);
+    f[i + 1] = make_float2(t.z, t.w);
+  }
+}
+
 // Load / store VEC consecutive elements as floats.  VEC == Vec16<T>::N uses a
 // single 16-byte access (streaming cache hint for activations); VEC == 1 is
 // the scalar path for ragged shapes.

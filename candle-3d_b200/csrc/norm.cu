@@ -109,6 +109,7 @@ template <typename T, int VEC, int G, int kNV, bool RES, bool STG>
 __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
     rownorm_kernel(const RowNormParams p) {
   using S = typename Packed<T, VEC>::S;
+  constexpr int P = VEC > 1 ? VEC / 2 : 1;  // float pairs per vector
   __shared__ float red[kBlock / 32];
   extern __shared__ float coef[];  // STG: [nbatch, C] A, [nbatch, C] Bc, [nbatch, C] gate
   if constexpr (STG) {
@@ -180,66 +181,95 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
     for (int i = 0; i < kNV; ++i) {
       const int64_t vi = tid + int64_t(i) * G;
       if (valid && vi < nvec) {
-        float a[VEC], hv[VEC];
-        unpack_v<T, VEC>(v[i], a);
-        unpack_v<T, VEC>(hp[i], hv);
-        if (p.g1.ptr) {
-          float g[VEC];
-          load_chan<VEC>(p.g1, b, vi * VEC, g);
+        if constexpr (VEC == 1) {
+          float a = v[i], hv = hp[i];
+          if (p.g1.ptr) {
+            float g[1];
+            load_chan<1>(p.g1, b, vi, g);
+            hv = hv * g[0];
+          }
+          float o[1] = {a + hv};
+          v[i] = pack_v<T, 1>(o);
+        } else {
+          float2 a[P], hv[P];
+          unpack2(v[i], a, T());
+          unpack2(hp[i], hv, T());
+          if (p.g1.ptr) {
+            float g[VEC];
+            load_chan<VEC>(p.g1, b, vi * VEC, g);
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) hv[e] = hv[e] * g[e];
+            for (int k = 0; k < P; ++k) a[k] = fma2(hv[k], make_float2(g[2 * k], g[2 * k + 1]), a[k]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < P; ++k) a[k] = add2(a[k], hv[k]);
+          }
+          v[i] = pack2(a, T());
         }
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) a[e] = a[e] + hv[e];
-        v[i] = pack_v<T, VEC>(a);
         if (rr) st_packed<T, VEC>(rr + vi * VEC, v[i]);
       }
     }
   }
 
+  // Statistics: LayerNorm mean, then the centred sum of squares (two passes
+  // over the registers); RMSNorm sum of squares.  Padding vectors are zero.
   float inv = 1.f, mean = 0.f;
   if (p.norm == NORM_LAYER) {
-    float s = 0.f;
+    float2 acc = f2(0.f);
 #pragma unroll
     for (int i = 0; i < kNV; ++i) {
-      float a[VEC];
-      unpack_v<T, VEC>(v[i], a);
+      if constexpr (VEC == 1) {
+        acc.x += v[i];
+      } else {
+        float2 a[P];
+        unpack2(v[i], a, T());
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) s += a[e];
+        for (int k = 0; k < P; ++k) acc = add2(acc, a[k]);
+      }
     }
-    s = group_sum<G>(s, red);
+    const float s = group_sum<G>(acc.x + acc.y, red);
     mean = s / float(p.C);
-    float ss = 0.f;
+    const float2 nm = f2(-mean);
+    acc = f2(0.f);
 #pragma unroll
     for (int i = 0; i < kNV; ++i) {
       const int64_t vi = tid + int64_t(i) * G;
       if (vi < nvec) {
-        float a[VEC];
-        unpack_v<T, VEC>(v[i], a);
+        if constexpr (VEC == 1) {
+          const float d = v[i] - mean;
+          acc.x += d * d;
+        } else {
+          float2 a[P];
+          unpack2(v[i], a, T());
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float d = a[e] - mean;
-          ss += d * d;
+          for (int k = 0; k < P; ++k) {
+            const float2 d = add2(a[k], nm);
+            acc = fma2(d, d, acc);
+          }
         }
       }
     }
-    ss = group_sum<G>(ss, red);
+    const float ss = group_sum<G>(acc.x + acc.y, red);
     inv = 1.f / sqrtf(ss / float(p.C) + p.eps);
   } else if (p.norm == NORM_RMS) {
-    float ss = 0.f;
+    float2 acc = f2(0.f);
 #pragma unroll
     for (int i = 0; i < kNV; ++i) {
-      float a[VEC];
-      unpack_v<T, VEC>(v[i], a);
+      if constexpr (VEC == 1) {
+        acc.x += v[i] * v[i];
+      } else {
+        float2 a[P];
+        unpack2(v[i], a, T());
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) ss += a[e] * a[e];
+        for (int k = 0; k < P; ++k) acc = fma2(a[k], a[k], acc);
+      }
     }
-    ss = group_sum<G>(ss, red);
+    const float ss = group_sum<G>(acc.x + acc.y, red);
     inv = 1.f / sqrtf(ss / float(p.C) + p.eps);
   }
   if (!valid) continue;
 
   T* yr = static_cast<T*>(p.y) + row_offset(p.ym, row);
+  const float2 nm = f2(-mean), inv2 = f2(inv);
 #pragma unroll
   for (int i = 0; i < kNV; ++i) {
     const int64_t vi = tid + int64_t(i) * G;
@@ -249,12 +279,35 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
       continue;
     }
     const int64_t c0 = vi * VEC;
+    if constexpr (STG && VEC > 1) {
+      // Folded per-channel coefficients: n * A + Bc [then gate, + input].
+      float2 a[P], o[P], fa[P], fb[P];
+      unpack2(v[i], a, T());
+#pragma unroll
+      for (int k = 0; k < P; ++k) o[k] = mul2(add2(a[k], nm), inv2);
+      const float* ca = coef + (p.nbatch > 1 ? b : 0) * p.C + c0;
+      const float* cb = ca + p.nbatch * p.C;
+      ld_pairs<P>(ca, fa);
+      ld_pairs<P>(cb, fb);
+#pragma unroll
+      for (int k = 0; k < P; ++k) o[k] = fma2(o[k], fa[k], fb[k]);
+      if (p.g2.ptr) {
+        ld_pairs<P>(cb + p.nbatch * p.C, fa);
+#pragma unroll
+        for (int k = 0; k < P; ++k) o[k] = mul2(fa[k], o[k]);
+      }
+      if (p.add_input) {
+#pragma unroll
+        for (int k = 0; k < P; ++k) o[k] = add2(o[k], a[k]);
+      }
+      st_packed<T, VEC>(yr + c0, pack2(o, T()));
+      continue;
+    }
     float a[VEC], o[VEC], t[VEC];
     unpack_v<T, VEC>(v[i], a);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) o[e] = (a[e] - mean) * inv;
     if constexpr (STG) {
-      // Folded per-channel coefficients: o * A + Bc [then gate, + input].
       const float* ca = coef + (p.nbatch > 1 ? b : 0) * p.C + c0;
       const float* cb = ca + p.nbatch * p.C;
       float fa[VEC], fb[VEC];

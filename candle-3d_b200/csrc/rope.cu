@@ -108,9 +108,7 @@ template <typename T>
 __device__ __forceinline__ typename Raw4<T>::type load_raw4(const T* p) {
   return __ldcs(reinterpret_cast<const typename Raw4<T>::type*>(p));
 }
-// Packed f32x2 arithmetic (FFMA2 / FADD2 / FMUL2 on sm_100): two
-// independent IEEE round-to-nearest operations per instruction.
-__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+// Elements 2 pr and 2 pr + 1 of a 4-element array as a float pair.
 __device__ __forceinline__ float2 as_f2(const float (&f)[4], int pr) {
   return make_float2(f[2 * pr], f[2 * pr + 1]);
 }
@@ -413,10 +411,16 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2) rope3d_kernel(con
   const int half = p.D / 2;
   const bool lane_on = m * EPL < p.D;
 
+  // The packed 16-bit path (PK) works on (re, re) and (im, im) pairs of two
+  // neighbouring rotation pairs, so gamma is staged in that order: each group
+  // of 4 elements (re0, im0, re1, im1) is stored as (re0, re1, im0, im1).
+  constexpr bool PK = EPL == 8 && sizeof(T) == 2;
   if (p.gamma) {
     for (int i = threadIdx.x; i < p.H * p.D; i += blockDim.x) {
       const int h = i / p.D, d = i - h * p.D;
-      gsm[i] = p.gamma[int64_t(h) * p.gsh + d] * p.scale;
+      int dst = i;
+      if constexpr (PK) dst = h * p.D + (d & ~3) + ((d & 1) << 1) + ((d >> 1) & 1);
+      gsm[dst] = p.gamma[int64_t(h) * p.gsh + d] * p.scale;
     }
     __syncthreads();
   }
@@ -485,6 +489,68 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 3 : 2) rope3d_kernel(con
         if (hb + it * HPI >= p.H) break;  // warp-uniform
         const int h = hb + it * HPI + hg;
         const bool valid = h < p.H && lane_on;
+        if constexpr (PK) {
+          // Pairs k = 0..3 of the lane (word k = (re_k, im_k)) as
+          // re2[q] = (re_2q, re_2q+1) and im2[q] = (im_2q, im_2q+1).
+          const uint32_t w[4] = {pk[it].u[0].x, pk[it].u[0].y, pk[it].u[0].z, pk[it].u[0].w};
+          float2 re2[2], im2[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+              re2[q] = make_float2(__uint_as_float(w[2 * q] << 16), __uint_as_float(w[2 * q + 1] << 16));
+              im2[q] = make_float2(__uint_as_float(w[2 * q] & 0xffff0000u),
+                                   __uint_as_float(w[2 * q + 1] & 0xffff0000u));
+            } else {
+              const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * q]));
+              const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * q + 1]));
+              re2[q] = make_float2(a.x, c.x);
+              im2[q] = make_float2(a.y, c.y);
+            }
+          }
+          if (p.gamma) {
+            float2 acc = mul2(re2[0], re2[0]);
+            acc = fma2(im2[0], im2[0], acc);
+            acc = fma2(re2[1], re2[1], acc);
+            acc = fma2(im2[1], im2[1], acc);
+            float ss = acc.x + acc.y;
+#pragma unroll
+            for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            // 1 / clamp(||x||, 1e-12, 1e30) = rsqrt(clamp(||x||^2, 1e-24, 1e60)).
+            const float2 rn = f2(rsqrtf(fminf(fmaxf(ss, 1e-24f), 1e30f * 1e30f)));
+            if (valid) {
+              const float4* g = reinterpret_cast<const float4*>(gsm + h * p.D + m * EPL);
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                const float4 gq = g[q];
+                re2[q] = mul2(re2[q], mul2(make_float2(gq.x, gq.y), rn));
+                im2[q] = mul2(im2[q], mul2(make_float2(gq.z, gq.w), rn));
+              }
+            }
+          }
+          // (re, im) -> (re c - im s, re s + im c).
+          uint32_t ow[4];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float2 c2 = make_float2(cs[2 * q], cs[2 * q + 1]);
+            const float2 s2 = make_float2(sn[2 * q], sn[2 * q + 1]);
+            const float2 ore = fma2(re2[q], c2, mul2(im2[q], make_float2(-s2.x, -s2.y)));
+            const float2 oim = fma2(re2[q], s2, mul2(im2[q], c2));
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+              __nv_bfloat162 h0 = __floats2bfloat162_rn(ore.x, oim.x);
+              __nv_bfloat162 h1 = __floats2bfloat162_rn(ore.y, oim.y);
+              ow[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
+              ow[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
+            } else {
+              __half2 h0 = __floats2half2_rn(ore.x, oim.x);
+              __half2 h1 = __floats2half2_rn(ore.y, oim.y);
+              ow[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
+              ow[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
+            }
+          }
+          if (valid)
+            __stcs(reinterpret_cast<uint4*>(yt + int64_t(h) * p.ysh), make_uint4(ow[0], ow[1], ow[2], ow[3]));
+          continue;
+        }
         float v[EPL];
         if constexpr (EPL == 8) unpack8<T>(pk[it], v);
         else { v[0] = sv[it][0]; v[1] = sv[it][1]; }

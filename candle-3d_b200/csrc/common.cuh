@@ -140,6 +140,14 @@ __device__ __forceinline__ uint4 pack(const float (&f)[8], __half) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Activation loads and stores of the streaming kernels: plain cached
+// accesses.  The evict-first (.cs) hints were measured slower on B200 for
+// these read-once / write-once sweeps (GELU 5.9 -> 6.3 TB/s without them).
+template <typename V>
+__device__ __forceinline__ V ld_act_raw(const V* p) { return *p; }
+template <typename V>
+__device__ __forceinline__ void st_act_raw(V* p, const V& v) { *p = v; }
+
 // Packed f32x2 arithmetic (FADD2 / FMUL2 / FFMA2 on sm_100): two independent
 // IEEE round-to-nearest operations per instruction, so element-wise work in
 // the HBM-bound kernels costs half the issue slots.
@@ -199,12 +207,11 @@ __device__ __forceinline__ void ld_pairs(const float* p, float2 (&f)[P]) {
 }
 
 // Load / store VEC consecutive elements as floats.  VEC == Vec16<T>::N uses a
-// single 16-byte access (streaming cache hint for activations); VEC == 1 is
-// the scalar path for ragged shapes.
+// single 16-byte access; VEC == 1 is the scalar path for ragged shapes.
 template <typename T, int VEC>
 __device__ __forceinline__ void load_act(const T* p, float (&f)[VEC]) {
   if constexpr (VEC == Vec16<T>::N) {
-    uint4 u = __ldcs(reinterpret_cast<const uint4*>(p));
+    uint4 u = ld_act_raw(reinterpret_cast<const uint4*>(p));
     unpack(u, f, T());
   } else {
 #pragma unroll
@@ -224,7 +231,7 @@ __device__ __forceinline__ void load_reuse(const T* p, float (&f)[VEC]) {
 template <typename T, int VEC>
 __device__ __forceinline__ void store_act(T* p, const float (&f)[VEC]) {
   if constexpr (VEC == Vec16<T>::N) {
-    __stcs(reinterpret_cast<uint4*>(p), pack(f, T()));
+    st_act_raw(reinterpret_cast<uint4*>(p), pack(f, T()));
   } else {
 #pragma unroll
     for (int i = 0; i < VEC; ++i) p[i] = from_f<T>(f[i]);

@@ -68,7 +68,7 @@ template <typename T> struct Packed<T, 1> { using S = float; };
 template <typename T, int VEC>
 __device__ __forceinline__ typename Packed<T, VEC>::S ld_packed(const T* p) {
   if constexpr (VEC == 1) return to_f(p[0]);
-  else return __ldcs(reinterpret_cast<const uint4*>(p));
+  else return ld_act_raw(reinterpret_cast<const uint4*>(p));
 }
 template <typename T, int VEC>
 __device__ __forceinline__ void unpack_v(const typename Packed<T, VEC>::S& s, float (&f)[VEC]) {
@@ -84,7 +84,7 @@ __device__ __forceinline__ typename Packed<T, VEC>::S pack_v(const float (&f)[VE
 template <typename T, int VEC>
 __device__ __forceinline__ void st_packed(T* p, const typename Packed<T, VEC>::S& s) {
   if constexpr (VEC == 1) p[0] = from_f<T>(s);
-  else __stcs(reinterpret_cast<uint4*>(p), s);
+  else st_act_raw(reinterpret_cast<uint4*>(p), s);
 }
 
 template <int VEC>
@@ -210,10 +210,52 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
     }
   }
 
-  // Statistics: LayerNorm mean, then the centred sum of squares (two passes
-  // over the registers); RMSNorm sum of squares.  Padding vectors are zero.
+  // Statistics: LayerNorm shifted moments in one pass (vector path, row within
+  // one warp) or mean then centred sum of squares (two passes); RMSNorm sum of
+  // squares.  Padding vectors are zero.
   float inv = 1.f, mean = 0.f;
-  if (p.norm == NORM_LAYER) {
+  bool stats_done = false;
+  if constexpr (G <= 32 && VEC > 1) {
+    if (p.norm == NORM_LAYER) {
+      stats_done = true;
+      // One pass of shifted moments: with K the row's first element (from the
+      // group's first thread), S1 = sum(x - K), S2 = sum((x - K)^2);
+      // mean = K + S1 / C, var = S2 / C - (S1 / C)^2.  K lies within the row's
+      // range, so the subtraction loses no more than the centred two-pass form
+      // for ordinary rows.
+      float2 a0[P];
+      unpack2(v[0], a0, T());
+      const int lane = threadIdx.x & 31;
+      const float K = __shfl_sync(0xffffffffu, a0[0].x, lane & ~(G - 1));
+      const float2 nk = f2(-K);
+      float2 s1 = f2(0.f), s2 = f2(0.f);
+#pragma unroll
+      for (int i = 0; i < kNV; ++i) {
+        const int64_t vi = tid + int64_t(i) * G;
+        if (vi < nvec) {
+          float2 a[P];
+          unpack2(v[i], a, T());
+#pragma unroll
+          for (int k = 0; k < P; ++k) {
+            const float2 d = add2(a[k], nk);
+            s1 = add2(s1, d);
+            s2 = fma2(d, d, s2);
+          }
+        }
+      }
+      float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+#pragma unroll
+      for (int o = (G < 32 ? G : 32) / 2; o > 0; o >>= 1) {
+        t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+        t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+      }
+      const float m1 = t1 / float(p.C);
+      mean = K + m1;
+      inv = 1.f / sqrtf(fmaxf(t2 / float(p.C) - m1 * m1, 0.f) + p.eps);
+    }
+  }
+  if (stats_done) {
+  } else if (p.norm == NORM_LAYER) {
     float2 acc = f2(0.f);
 #pragma unroll
     for (int i = 0; i < kNV; ++i) {

@@ -205,7 +205,7 @@ __global__ void index_select_kernel(const T* __restrict__ feats, int64_t fs0, in
     if (vec) {
       for (int64_t c = int64_t(lane) * V; c < C; c += 32 * V) {
         uint4 u = ok ? __ldg(reinterpret_cast<const uint4*>(f + c)) : make_uint4(0, 0, 0, 0);
-        __stcs(reinterpret_cast<uint4*>(o + c), u);
+        st_act_raw(reinterpret_cast<uint4*>(o + c), u);
       }
     } else {
       for (int64_t c = lane; c < C; c += 32) o[c] = ok ? f[c] : from_f<T>(0.f);

@@ -122,14 +122,18 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def ncu_traffic(kernel_key):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+def ncu_traffic(kernel_key, rows):
+    """DRAM bytes (read + write) of one launch of `kernel_key` ("name@C") over
+    `rows` token rows, scaled from the committed ncu measurement (traffic is
+    proportional to rows); None when that kernel/width was not captured."""
     p = ROOT / "profiles" / "ncu_traffic.json"
     if not p.exists():
         return None
     try:
-        return json.loads(p.read_text()).get(kernel_key)
-    except (ValueError, OSError):
+        d = json.loads(p.read_text())
+        v = d.get("bytes_per_launch", {}).get(kernel_key)
+        return None if v is None else int(round(v * rows / d["rows"]))
+    except (ValueError, OSError, KeyError):
         return None
 
 
@@ -627,7 +631,7 @@ def main():
     dom = max(per, key=per.get)
     peak, peak_kind = measured_peaks()
     ach = 4.0 * T * C / (per[dom] / 1e3) / 1e9
-    traffic = ncu_traffic(dom)
+    traffic = ncu_traffic(f"{dom}@{C}", T)
 
     # ---- end to end through the C ABI with host buffers
     e2e = None

@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
+    ap.add_argument("--qfmt", default="q8_0", choices=["q8_0", "q4_k", "q5_k", "q6_k"],
+                    help="qlinear workload: weight format (q8_0 is config 4's)")
     ap.add_argument("--workload", default="chain",
                     choices=["chain", "vggt", "triposg", "trellis", "qlinear"],
                     help="chain: config 5 fused layer-op chain (GB/s); vggt / triposg / "
@@ -379,7 +381,10 @@ def run_qlinear(args, local):
     g = torch.Generator().manual_seed(20261201)
     M = 31500
     shapes = [(4608, 1536), (1536, 1536), (8192, 1536), (1536, 8192)]
-    mms = [blocks._q8_linear(g, n, k, dev) for n, k in shapes]
+    if args.qfmt == "q8_0":
+        mms = [blocks._q8_linear(g, n, k, dev) for n, k in shapes]
+    else:
+        mms = [blocks._kq_linear(g, args.qfmt, n, k, dev) for n, k in shapes]
     xs = {k: torch.randn(M, k, generator=g).to(dev, torch.bfloat16) for k in {1536, 8192}}
     flops = sum(2.0 * M * n * k for n, k in shapes)
 
@@ -410,9 +415,9 @@ def run_qlinear(args, local):
         "metric": "dequant-linear TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 (Q8_0 weights)", "data": "synthetic (seeded)",
+        "vs_baseline": None, "dtype": f"bf16 ({args.qfmt.upper()} weights)", "data": "synthetic (seeded)",
         "config": {"workload": "config4 block linears: M=31500 x (4608x1536, 1536x1536, "
-                               "8192x1536, 1536x8192), Q8_0", "baseline_metric": BASELINE_METRIC},
+                               f"8192x1536, 1536x8192), {args.qfmt.upper()}", "baseline_metric": BASELINE_METRIC},
         "roofline": {"bound": "tensor", "kernel": "qgemm_kernel (decode included)",
                      "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(tf / peak, 4), "traffic": None},

@@ -20,7 +20,7 @@ HEADER = PKG.parent / "include" / "l3d_ops.h"
 
 MAX_DIMS = 6
 F32, F16, BF16, I32, I64, U32, U8 = 0, 1, 2, 3, 4, 5, 6
-Q8_0, Q4_0 = 8, 2
+Q8_0, Q4_0, Q4_K, Q5_K, Q6_K = 8, 2, 12, 13, 14
 STATUS = {0: "OK", 1: "E_SHAPE", 2: "E_DTYPE", 3: "E_ALIGN", 4: "E_UNSUPPORTED", 5: "E_CUDA",
           6: "E_NULL", 7: "E_WORKSPACE", 8: "E_DEVICE"}
 

@@ -306,6 +306,30 @@ def _q8_linear(g, n, k, dev, scale_lo=0.001, scale_hi=0.02):
     return ops.QMatMul(blocks.to(dev), "q8_0", n, k, bias=b.to(dev))
 
 
+KQ_BLOCK_BYTES = {"q4_k": 144, "q5_k": 176, "q6_k": 210}
+
+
+def _kq_linear(g, fmt, n, k, dev):
+    """Synthetic GGML K-quant weight ([n, k], k % 256 == 0): random quant bits
+    and 6-bit scales / mins (Q6_K int8 scales in [-16, 16]), f16 super-block
+    scales ~ U(1e-4, 1e-3); plus its f32 bias."""
+    nsb = n * (k // 256)
+    bb = KQ_BLOCK_BYTES[fmt]
+    blk = torch.randint(0, 256, (nsb, bb), generator=g, dtype=torch.int32).to(torch.uint8)
+    d = torch.empty(nsb).uniform_(1e-4, 1e-3, generator=g).to(torch.float16).view(torch.uint8)
+    d = d.reshape(nsb, 2)
+    if fmt == "q6_k":
+        sc = torch.randint(-16, 17, (nsb, 16), generator=g, dtype=torch.int32).to(torch.int8)
+        blk[:, 192:208] = sc.view(torch.uint8)
+        blk[:, 208:210] = d
+    else:
+        dm = torch.empty(nsb).uniform_(1e-4, 1e-3, generator=g).to(torch.float16)
+        blk[:, 0:2] = d
+        blk[:, 2:4] = dm.view(torch.uint8).reshape(nsb, 2)
+    b = (0.02 * torch.randn(n, generator=g)).float()
+    return ops.QMatMul(blk.reshape(-1).contiguous().to(dev), fmt, n, k, bias=b.to(dev))
+
+
 def quantize_q8_0_torch(w: torch.Tensor) -> torch.Tensor:
     """GGML quantize_row_q8_0 (d = amax / 127, q = round(w / d)) on the host."""
     n, k = w.shape

@@ -713,13 +713,15 @@ static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 constexpr int64_t kDecodeOnceRows = 512;
 
 // Workspace: [0, 256) status word; a bf16 copy of the activations (used when
-// x is F32 or its rows are not 16-byte aligned); for m > kDecodeOnceRows the
-// decoded bf16 weights [n, k].
+// x is F32 or its rows are not 16-byte aligned); for m > kDecodeOnceRows, and
+// always for the K-quants (256-weight super-blocks), the decoded bf16 weights
+// [n, k].
+static bool decode_once(int fmt, int64_t m) { return m > kDecodeOnceRows || is_kquant(fmt); }
+
 extern "C" size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t n, int64_t k) {
-  (void)fmt;
   if (m < 0 || k < 0 || n < 0) return 0;
   size_t bytes = 256 + align256(size_t(m) * size_t(k) * 2);
-  if (m > kDecodeOnceRows) bytes += align256(size_t(n) * size_t(k) * 2);
+  if (decode_once(fmt, m)) bytes += align256(size_t(n) * size_t(k) * 2);
   return bytes;
 }
 
@@ -730,12 +732,13 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
   using namespace l3d::gemm;
   if (!x || !y || !wq || no_data(x) || no_data(y))
     return fail(L3D_E_NULL, "%s: x, wq and y are required", op);
-  if (fmt != L3D_Q8_0 && fmt != L3D_Q4_0) return fail(L3D_E_UNSUPPORTED, "%s: unknown format", op);
+  if (!qfmt_known(fmt)) return fail(L3D_E_UNSUPPORTED, "%s: unknown format", op);
   if (x->dtype != L3D_BF16 && x->dtype != L3D_F32)
     return fail(L3D_E_DTYPE, "%s: x must be BF16 or F32", op);
   if (y->dtype != L3D_BF16 && y->dtype != L3D_F32)
     return fail(L3D_E_DTYPE, "%s: y must be BF16 or F32", op);
-  if (k <= 0 || k % 32 || n <= 0) return fail(L3D_E_SHAPE, "%s: k must be a positive multiple of 32", op);
+  if (k <= 0 || k % block_elems(fmt) || n <= 0)
+    return fail(L3D_E_SHAPE, "%s: k must be a positive multiple of %d", op, block_elems(fmt));
   if (x->ndim < 1 || x->dims[x->ndim - 1] != k) return fail(L3D_E_SHAPE, "%s: x last dim != k", op);
   if (y->ndim != x->ndim || y->dims[y->ndim - 1] != n) return fail(L3D_E_SHAPE, "%s: y last dim != n", op);
   int64_t M = 1;
@@ -800,7 +803,7 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
   p.status = status;
   p.wq = static_cast<const uint8_t*>(wq);
   p.fmt = fmt;
-  p.row_bytes = (k / 32) * block_bytes(fmt);
+  p.row_bytes = (k / block_elems(fmt)) * block_bytes(fmt);
   p.bpt = 2 * block_bytes(fmt);
   CUtensorMap map_x, map_w, map_y;
   if (!make_map_x(&map_x, xa, uint64_t(M), uint64_t(k), uint64_t(lda)))
@@ -814,7 +817,7 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
                     : 0;
   if (!p.tma_store) map_y = map_x;  // unused
   int mode;
-  if (M > kDecodeOnceRows) {
+  if (decode_once(fmt, M)) {
     // Decode the weights once into the workspace (bf16 [n, k]), then stream
     // them with TMA like the activations.
     char* wb = ws + 256 + align256(size_t(M) * size_t(k) * 2);

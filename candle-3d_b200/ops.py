@@ -278,8 +278,10 @@ def patch_embed(pixels, weight, bias, pos, cls, reg, patch: int):
 
 
 # ------------------------------------------------------------- dequant-linear
-QFMT = {"q8_0": _lib.Q8_0, "q4_0": _lib.Q4_0}
-BLOCK_BYTES = {"q8_0": 34, "q4_0": 18}
+QFMT = {"q8_0": _lib.Q8_0, "q4_0": _lib.Q4_0, "q4_k": _lib.Q4_K, "q5_k": _lib.Q5_K,
+        "q6_k": _lib.Q6_K}
+BLOCK_BYTES = {"q8_0": 34, "q4_0": 18, "q4_k": 144, "q5_k": 176, "q6_k": 210}
+BLOCK_ELEMS = {"q8_0": 32, "q4_0": 32, "q4_k": 256, "q5_k": 256, "q6_k": 256}
 
 
 def dequantize(wq, fmt: str, n: int, k: int, dtype=torch.float32):
@@ -296,7 +298,7 @@ class QMatMul:
 
     def __init__(self, blocks, fmt: str, n: int, k: int, bias=None):
         _check_cuda(blocks, bias)
-        if blocks.numel() != n * (k // 32) * BLOCK_BYTES[fmt]:
+        if blocks.numel() != n * (k // BLOCK_ELEMS[fmt]) * BLOCK_BYTES[fmt]:
             raise ValueError("block buffer size does not match [n, k]")
         self.blocks, self.fmt, self.n, self.k, self.bias = blocks, fmt, n, k, bias
         self._ws = None

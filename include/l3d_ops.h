@@ -251,13 +251,26 @@ int l3d_patch_embed(const l3d_tensor* pixels, const l3d_tensor* weight,
                     const l3d_tensor* reg, int patch, const l3d_tensor* out,
                     l3d_stream stream);
 
-/* ---- a13: dequant-linear on GGML Q8_0 / Q4_0 blocks --------------------------- */
+/* ---- a13: dequant-linear on GGML Q8_0 / Q4_0 / K-quant blocks ------------------ */
 
-typedef enum l3d_qfmt { L3D_Q8_0 = 8, L3D_Q4_0 = 2 } l3d_qfmt;
+/* Values are the GGML type ids (GgmlDType in candle_core::quantized, the
+ * dtypes crate/weights/quantize.rs:355-373 names). */
+typedef enum l3d_qfmt {
+  L3D_Q8_0 = 8, L3D_Q4_0 = 2,
+  L3D_Q4_K = 12, L3D_Q5_K = 13, L3D_Q6_K = 14
+} l3d_qfmt;
 
-/* QTensor::dequantize for a [N, K] Q8_0 / Q4_0 block matrix (GGML layout:
- * Q8_0 = {f16 d; int8 q[32]} 34 B, w = d*q; Q4_0 = {f16 d; u8 qs[16]} 18 B,
- * w = d*((nibble) - 8), low nibbles hold elements 0..15, high 16..31).
+/* QTensor::dequantize for a [N, K] block matrix in the GGML public layouts:
+ *  Q8_0 = {f16 d; int8 q[32]} 34 B, w = d*q;
+ *  Q4_0 = {f16 d; u8 qs[16]} 18 B, w = d*((nibble) - 8), low nibbles hold
+ *         elements 0..15, high 16..31;
+ *  256-weight super-blocks (K % 256 == 0):
+ *  Q4_K = {f16 d; f16 dmin; u8 scales[12]; u8 qs[128]} 144 B, 8 sub-blocks of
+ *         32 with 6-bit scale sc and min m, w = (d*sc)*q - dmin*m;
+ *  Q5_K = {f16 d; f16 dmin; u8 scales[12]; u8 qh[32]; u8 qs[128]} 176 B,
+ *         as Q4_K with a fifth bit from qh;
+ *  Q6_K = {u8 ql[128]; u8 qh[64]; int8 scales[16]; f16 d} 210 B,
+ *         w = (d*sc)*(q - 32) with 6-bit q and 16 sub-blocks of 16.
  * out: [N, K] F32/BF16/F16 contiguous. */
 int l3d_dequantize(const void* wq, int fmt, int64_t n, int64_t k, const l3d_tensor* out,
                    l3d_stream stream);
@@ -268,7 +281,9 @@ size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t n, int64_t 
 /* y[M, N] = x[M, K] . deq(W)^T + bias  (Linear::forward / QMatMul::forward,
  * crate/runtime/nn_blocks.rs:80-95, weights from quantized_linear :123-152).
  * x: [.., K] BF16 (F32 accepted: rounded to BF16 on the way in), contiguous
- * rows; W: raw GGML blocks (n rows of k/32 blocks); bias [N] F32/BF16 or NULL;
+ * rows; W: raw GGML blocks (n rows of k/32 blocks, or k/256 super-blocks for
+ * the K-quants, which are always decoded once per call into the workspace);
+ * bias [N] F32/BF16 or NULL;
  * y: [.., N] BF16 or F32 contiguous.  Tensor cores (tcgen05, TMEM
  * accumulators, f32 accumulate). */
 int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n, int64_t k,

@@ -429,7 +429,86 @@ static uint16_t f2h(float f) {
 }
 
 /* GGML block decode (public format; QTensor::dequantize). */
+/* GGML K-quant super-blocks (256 weights), public layouts and decode order
+ * (dequantize_row_q4_K / _q5_K / _q6_K in ggml; Candle's k_quants follow
+ * them): Q4_K {f16 d, f16 dmin, u8 scales[12], u8 qs[128]} 144 B; Q5_K adds
+ * u8 qh[32] before qs, 176 B; Q6_K {u8 ql[128], u8 qh[64], i8 scales[16],
+ * f16 d} 210 B.  The f32 products and differences are formed one at a time
+ * (no contraction), in the order written here. */
+static void kq_scale_min(const uint8_t* q, int j, int* sc, int* m) {
+  if (j < 4) {
+    *sc = q[j] & 63;
+    *m = q[j + 4] & 63;
+  } else {
+    *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+static void dequant_q45k_block(const uint8_t* blk, int q5, float* y) {
+  const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+  const float dmin = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
+  const uint8_t* scales = blk + 4;
+  const uint8_t* qh = blk + 16;
+  const uint8_t* ql = blk + (q5 ? 48 : 16);
+  int is = 0;
+  for (int j = 0; j < 256; j += 64) {
+    int sc, m;
+    kq_scale_min(scales, is, &sc, &m);
+    const float d1 = d * (float)sc, m1 = dmin * (float)m;
+    kq_scale_min(scales, is + 1, &sc, &m);
+    const float d2 = d * (float)sc, m2 = dmin * (float)m;
+    const int b1 = is, b2 = is + 1; /* qh bit of the two sub-blocks */
+    for (int l = 0; l < 32; ++l) {
+      int q = ql[l] & 0xF;
+      if (q5) q += ((qh[l] >> b1) & 1) << 4;
+      *y++ = d1 * (float)q - m1;
+    }
+    for (int l = 0; l < 32; ++l) {
+      int q = ql[l] >> 4;
+      if (q5) q += ((qh[l] >> b2) & 1) << 4;
+      *y++ = d2 * (float)q - m2;
+    }
+    ql += 32;
+    is += 2;
+  }
+}
+
+static void dequant_q6k_block(const uint8_t* blk, float* y) {
+  const uint8_t* ql = blk;
+  const uint8_t* qh = blk + 128;
+  const int8_t* sc = (const int8_t*)(blk + 192);
+  const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+  for (int n = 0; n < 256; n += 128) {
+    for (int l = 0; l < 32; ++l) {
+      const int is = l / 16;
+      const int q1 = (int)((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+      const int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+      const int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+      const int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+      y[l] = d * (float)sc[is + 0] * (float)q1;
+      y[l + 32] = d * (float)sc[is + 2] * (float)q2;
+      y[l + 64] = d * (float)sc[is + 4] * (float)q3;
+      y[l + 96] = d * (float)sc[is + 6] * (float)q4;
+    }
+    y += 128;
+    ql += 64;
+    qh += 32;
+    sc += 8;
+  }
+}
+
 int orc_dequantize(const uint8_t* wq, int fmt, int64_t n, int64_t k, float* out) {
+  if (fmt == 12 || fmt == 13 || fmt == 14) {
+    const int bb = fmt == 12 ? 144 : fmt == 13 ? 176 : 210;
+    if (k % 256) return 1;
+    const int64_t nsb = n * (k / 256);
+    for (int64_t b = 0; b < nsb; ++b) {
+      if (fmt == 14) dequant_q6k_block(wq + b * bb, out + b * 256);
+      else dequant_q45k_block(wq + b * bb, fmt == 13, out + b * 256);
+    }
+    return 0;
+  }
   const int bb = fmt == 8 ? 34 : 18;
   const int64_t nblk = n * (k / 32);
   for (int64_t b = 0; b < nblk; ++b) {

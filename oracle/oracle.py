@@ -49,8 +49,7 @@ _lib = None
 def lib():
     global _lib
     if _lib is None:
-        if not LIB.exists():
-            build()
+        build()  # compiles only when the library is missing or older than the source
         L = C.CDLL(str(LIB))
         sig = {
             "orc_round_array": [_f32p, _i64, _int],
@@ -314,8 +313,9 @@ def patch_embed(pixels, weight, bias, pos, cls, reg, patch):
 
 
 # ---------------------------------------------------------------- GGML blocks
-QFMT = {"q8_0": 8, "q4_0": 2}
-BLOCK_BYTES = {"q8_0": 34, "q4_0": 18}
+QFMT = {"q8_0": 8, "q4_0": 2, "q4_k": 12, "q5_k": 13, "q6_k": 14}
+BLOCK_BYTES = {"q8_0": 34, "q4_0": 18, "q4_k": 144, "q5_k": 176, "q6_k": 210}
+BLOCK_ELEMS = {"q8_0": 32, "q4_0": 32, "q4_k": 256, "q5_k": 256, "q6_k": 256}
 
 
 def quantize(w, fmt):

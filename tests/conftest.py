@@ -88,3 +88,24 @@ def assert_close(got, ref, dt: str, what: str = ""):
         i = np.unravel_index(np.argmax(err - bound), err.shape)
         raise AssertionError(f"{what} [{dt}]: {bad.sum()} of {err.size} outside tolerance; worst at "
                              f"{i}: got {got[i]} ref {ref[i]} (err {err[i]:.3e})")
+
+
+KQ_BYTES = {"q4_k": 144, "q5_k": 176, "q6_k": 210}
+
+
+def random_kquant_blocks(r: np.random.Generator, fmt: str, n: int, k: int) -> np.ndarray:
+    """Random GGML K-quant super-blocks for an [n, k] weight (k % 256 == 0):
+    random quant bits, random 6-bit scales / mins (int8 scales in [-16, 16]
+    for Q6_K) and f16 super-block scales d, dmin ~ U(1e-3, 1e-2)."""
+    nsb = n * (k // 256)
+    bb = KQ_BYTES[fmt]
+    blk = r.integers(0, 256, size=(nsb, bb), dtype=np.uint8)
+    d = r.uniform(1e-3, 1e-2, size=nsb).astype(np.float16).view(np.uint8).reshape(nsb, 2)
+    if fmt == "q6_k":
+        blk[:, 192:208] = r.integers(-16, 17, size=(nsb, 16)).astype(np.int8).view(np.uint8)
+        blk[:, 208:210] = d
+    else:
+        dm = r.uniform(1e-3, 1e-2, size=nsb).astype(np.float16).view(np.uint8).reshape(nsb, 2)
+        blk[:, 0:2] = d
+        blk[:, 2:4] = dm
+    return blk.reshape(-1)

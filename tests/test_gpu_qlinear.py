@@ -90,3 +90,46 @@ def test_dequant_linear_repeated_calls_are_deterministic(ops, orc, dev):
     assert torch.equal(y1, y2)
     ws = mm.workspace(M)
     assert int(ws[:4].view(torch.int32).item()) == 0  # kernel status word: no timeouts
+
+
+@pytest.mark.parametrize("fmt", ["q4_k", "q5_k", "q6_k"])
+def test_dequantize_kquants_bit_exact(ops, orc, dev, fmt):
+    """Device decode of K-quant super-blocks equals the oracle bit for bit
+    (f32 out), and its bf16 output is the oracle rounded once."""
+    import torch
+
+    from conftest import random_kquant_blocks
+
+    n, k = 96, 2048
+    blk = random_kquant_blocks(rng(500 + len(fmt)), fmt, n, k)
+    ref = orc.dequantize(blk, fmt, n, k)
+    q = torch.from_numpy(blk).to(dev)
+    got = ops.dequantize(q, fmt, n, k, dtype=torch.float32).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    gb = ops.dequantize(q, fmt, n, k, dtype=torch.bfloat16).float().cpu().numpy()
+    assert np.array_equal(gb, orc.round_bf16(ref))
+
+
+@pytest.mark.parametrize("M,N,K,fmt", [
+    (37, 512, 1024, "q4_k"),     # small M: K-quants decode once as well
+    (700, 1536, 1536, "q6_k"),   # TRELLIS to_out shape
+    (300, 768, 2048, "q5_k"),
+])
+def test_dequant_linear_kquants(ops, orc, dev, M, N, K, fmt):
+    import torch
+
+    from conftest import random_kquant_blocks
+
+    r = rng(600 + M)
+    x = r.standard_normal((M, K)).astype(np.float32)
+    blk = random_kquant_blocks(r, fmt, N, K)
+    b = (0.1 * r.standard_normal(N)).astype(np.float32)
+    xb = torch.from_numpy(x).to(dev).to(torch.bfloat16)
+    xv = xb.float().cpu().numpy().astype(np.float64)
+    wb = orc.round_bf16(orc.dequantize(blk, fmt, N, K)).astype(np.float64)
+    mm = ops.QMatMul(torch.from_numpy(blk).to(dev), fmt, N, K, bias=torch.from_numpy(b).to(dev))
+    y = mm(xb, out_dtype=torch.float32).cpu().numpy()
+    ref = xv @ wb.T + b
+    bound = 2e-5 * (np.abs(xv) @ np.abs(wb).T) + 1e-6
+    err = np.abs(y - ref)
+    assert np.all(err <= bound), f"max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"

@@ -3,8 +3,9 @@ candle-3d models behind a C ABI (libl3dops.so, include/l3d_ops.h).
 
 `ops` mirrors the Candle ops the reference model code calls; `_lib` is the
 ctypes binding of the C ABI; `blocks` assembles the VGGT, TripoSG and
-TRELLIS.2 block stacks from them; `shard` splits token rows across ranks.
+TRELLIS.2 block stacks from them; `gguf` indexes GGUF checkpoints for the
+dequant-linear; `shard` splits token rows across ranks.
 """
-from . import _lib, blocks, ops, shard  # noqa: F401
+from . import _lib, blocks, gguf, ops, shard  # noqa: F401
 
-__all__ = ["ops", "blocks", "shard", "_lib"]
+__all__ = ["ops", "blocks", "gguf", "shard", "_lib"]

@@ -103,7 +103,24 @@ _SIGS = {
     "l3d_sparse_neighbor_pairs": ([_P, _P, _P, _P, C.c_void_p, C.c_size_t, _S], C.c_int),
     "l3d_sparse_neighbor_pairs_noalloc": ([_P, _P, _P, _P, _S], C.c_int),
     "l3d_index_select_rows": ([_P, _P, _P, _S], C.c_int),
+    "l3d_gguf_index": ([C.c_void_p, C.c_uint64, C.c_void_p, C.c_int64, C.POINTER(C.c_int64),
+                        C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)], C.c_int),
+    "l3d_gguf_metadata_string": ([C.c_void_p, C.c_uint64, C.c_char_p, C.POINTER(C.c_void_p),
+                                  C.POINTER(C.c_uint64)], C.c_int),
 }
+
+
+class GgufTensorInfo(C.Structure):
+    """l3d_gguf_tensor (include/l3d_ops.h)."""
+    _fields_ = [
+        ("name", C.c_void_p),
+        ("name_len", C.c_uint64),
+        ("type", C.c_int32),
+        ("n_dims", C.c_int32),
+        ("dims", C.c_int64 * 4),
+        ("offset", C.c_uint64),
+        ("nbytes", C.c_uint64),
+    ]
 
 _lib = None
 

@@ -290,6 +290,39 @@ int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n, 
                        const l3d_tensor* bias, const l3d_tensor* y, void* workspace,
                        size_t workspace_bytes, l3d_stream stream);
 
+/* ---- GGUF tensor index (the on-disk format feeding a13) ------------------------ */
+
+/* One tensor of a GGUF file.  name points into the caller's buffer (not
+ * NUL-terminated); dims are in row-major (Candle) order, dims[0] outermost,
+ * unused trailing dims 1; offset is the byte offset of the data from the start
+ * of the buffer; nbytes is 0 for a GGML type this library does not know. */
+typedef struct l3d_gguf_tensor {
+  const char* name;
+  uint64_t name_len;
+  int32_t type;      /* GGML type id: 0 F32, 1 F16, 30 BF16, 2 Q4_0, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K, ... */
+  int32_t n_dims;
+  int64_t dims[4];
+  uint64_t offset;
+  uint64_t nbytes;
+} l3d_gguf_tensor;
+
+/* gguf_file::Content::read (Candle, used at crate/weights/mod.rs:596-650 on
+ * the file crate/weights/quantize.rs:255-295 writes): index a GGUF v2/v3
+ * buffer (e.g. an mmap of model.gguf).  Fills up to max_tensors entries
+ * (tensors may be NULL when max_tensors is 0) and stores the file's tensor
+ * count in *n_tensors; version / alignment (general.alignment, default 32)
+ * are optional outputs.  Host code only: no device work, no allocation;
+ * malformed or truncated buffers return L3D_E_SHAPE. */
+int l3d_gguf_index(const void* buf, uint64_t len, l3d_gguf_tensor* tensors,
+                   int64_t max_tensors, int64_t* n_tensors, uint32_t* version,
+                   uint64_t* alignment);
+
+/* The string value of metadata `key` (e.g. "general.architecture",
+ * "lux3d.family", "lux3d.resolved_config", crate/weights/mod.rs:26-28),
+ * pointing into buf; L3D_E_SHAPE when absent or not a string. */
+int l3d_gguf_metadata_string(const void* buf, uint64_t len, const char* key,
+                             const char** value, uint64_t* value_len);
+
 /* ---- a14: sparse voxel neighbour pairs and row gather ---------------------------- */
 
 /* Workspace bytes for l3d_sparse_neighbor_pairs on n coordinates. */

@@ -16,7 +16,7 @@ follows it:
   * TRELLIS.2 SLAT (crate/runtime/trellis2_blocks.rs:609-646,
     crate/runtime/trellis2_dit.rs:549-574): shared adaLN, modulated norms,
     L2-norm * gamma + 3D RoPE on integer voxel coordinates, Q8_0 weights through
-    the dequant-linear, tanh-GELU FFN.
+    the dequant-linear, tanh-GELU FFN (the GELU runs in mlp.0's GEMM epilogue).
 
 Weights are random (~N(0, 0.02)); there is no checkpoint loader here.
 `*_reference` functions restate each block in plain torch f32 (used by the
@@ -411,7 +411,7 @@ class Trellis2Slat:
             co = p["c_out"](ca.transpose(1, 2).reshape(1, N, C))
             x, y = ops.residual_layer_norm_modulate(x, co, shift=sh_mlp, scale=sc_mlp, eps=1e-6,
                                                     inplace=True)
-            h = p["mlp2"](ops.gelu(p["mlp0"](y)))
+            h = p["mlp2"](p["mlp0"](y, act="gelu"))  # tanh-GELU in mlp.0's epilogue
             if i + 1 < len(self.blocks):
                 x, y = ops.residual_layer_norm_modulate(x, h, gate=g_mlp, shift=mods[i + 1][0],
                                                         scale=mods[i + 1][1], eps=1e-6, inplace=True)

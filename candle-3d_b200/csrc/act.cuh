@@ -87,5 +87,13 @@ __device__ __forceinline__ float act_dyn(int a, float x) {
     default: return x;
   }
 }
+__device__ __forceinline__ float act_dyn_fast(int a, float x) {
+  switch (a) {
+    case ACT_SILU: return silu_fast(x);
+    case ACT_GELU_ERF: return gelu_erf_fast(x);
+    case ACT_GELU_TANH: return gelu_tanh_fast(x);
+    default: return x;
+  }
+}
 
 }  // namespace l3d

@@ -28,6 +28,7 @@
 
 #include <mutex>
 
+#include "act.cuh"
 #include "common.cuh"
 #include "qlinear.cuh"
 
@@ -258,7 +259,62 @@ struct Params {
   int fmt;
   int bpt;            // raw bytes per 64-wide K step (2 blocks)
   int tma_store;      // epilogue writes y through the map_y tensor map
+  // Fused epilogue: y = res + gate * act(acc + bias).
+  int act;            // Act code (0: none)
+  const void* res;    // [M, N] rows of res_ld elements, y's dtype; null: none
+  int64_t res_ld;
+  int res_vec;        // res rows are 16-byte aligned (vector loads)
+  const void* gate;   // [N] or null (= 1)
+  int gate_dtype;
 };
+
+// The fused epilogue ops on NC consecutive columns [col0, col0 + NC) of one
+// row, after the bias: the activation (the reduced-cost forms for 16-bit
+// outputs), then the gated residual, 8 columns at a time.  Columns past N are
+// left alone.
+template <int NC>
+__device__ __forceinline__ void epi_post(const Params& p, int row, int col0, float (&v)[NC]) {
+  if (p.act) {
+    const bool fast = p.y_dtype != L3D_F32;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) v[i] = fast ? act_dyn_fast(p.act, v[i]) : act_dyn(p.act, v[i]);
+  }
+  if (!p.res || row >= p.M) return;
+  const bool bf = p.y_dtype == L3D_BF16;
+  const char* rrow = static_cast<const char*>(p.res) + (int64_t(row) * p.res_ld + col0) * (bf ? 2 : 4);
+#pragma unroll
+  for (int q = 0; q < NC / 8; ++q) {
+    const int c = col0 + 8 * q;
+    if (c >= p.N) break;
+    float r[8], g[8];
+    if (c + 8 <= p.N && p.res_vec) {
+      if (bf) {
+        unpack(__ldg(reinterpret_cast<const uint4*>(rrow) + q), r, __nv_bfloat16());
+      } else {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(rrow) + 2 * q);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(rrow) + 2 * q + 1);
+        r[0] = a.x; r[1] = a.y; r[2] = a.z; r[3] = a.w; r[4] = b.x; r[5] = b.y; r[6] = b.z; r[7] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = c + e < p.N ? 8 * q + e : 8 * q;  // clamp to a valid column
+        r[e] = bf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rrow)[i])
+                  : __ldg(reinterpret_cast<const float*>(rrow) + i);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int col = c + e < p.N ? c + e : p.N - 1;
+      g[e] = !p.gate ? 1.f
+             : p.gate_dtype == L3D_F32 ? __ldg(static_cast<const float*>(p.gate) + col)
+                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(p.gate)[col]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (c + e < p.N) v[8 * q + e] = fmaf(g[e], v[8 * q + e], r[e]);
+  }
+}
 
 // int8 -> f32 exactly: place (q ^ 0x80) = q + 128 in the mantissa of 2^23.
 __device__ __forceinline__ float i8_to_f(uint32_t byte) {
@@ -496,6 +552,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
+          if (p.act || p.res) epi_post<EPI_COLS>(p, row, col0, v);
           // The previous stores from this staging area must have read it.
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
@@ -547,6 +604,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[col]);
             }
           }
+          if (p.act || p.res) epi_post<32>(p, row, col0, v);
           if (p.y_dtype == L3D_BF16) {
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + int64_t(row) * p.y_ld + col0;
             if (col0 + 32 <= p.N) {
@@ -725,10 +783,10 @@ extern "C" size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t 
   return bytes;
 }
 
-extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n,
-                                  int64_t k, const l3d_tensor* bias, const l3d_tensor* y,
-                                  void* workspace, size_t workspace_bytes, l3d_stream stream) {
-  const char* op = "l3d_dequant_linear";
+static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n, int64_t k,
+                              const l3d_tensor* bias, int act, const l3d_tensor* residual,
+                              const l3d_tensor* gate, const l3d_tensor* y, void* workspace,
+                              size_t workspace_bytes, l3d_stream stream, const char* op) {
   using namespace l3d::gemm;
   if (!x || !y || !wq || no_data(x) || no_data(y))
     return fail(L3D_E_NULL, "%s: x, wq and y are required", op);
@@ -764,6 +822,33 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
       return fail(L3D_E_SHAPE, "%s: bias must be contiguous [n]", op);
   }
   if (reinterpret_cast<uintptr_t>(wq) % 2) return fail(L3D_E_ALIGN, "%s: wq must be 2-byte aligned", op);
+  if (act < ACT_NONE || act > ACT_GELU_TANH) return fail(L3D_E_UNSUPPORTED, "%s: unknown activation", op);
+  const void* res_ptr = nullptr;
+  int64_t res_ld = 0;
+  int res_vec = 0;
+  if (residual) {
+    if (no_data(residual)) return fail(L3D_E_NULL, "%s: residual has no data", op);
+    if (residual->dtype != y->dtype) return fail(L3D_E_DTYPE, "%s: residual must have y's dtype", op);
+    if (residual->ndim != y->ndim) return fail(L3D_E_SHAPE, "%s: residual must have y's shape", op);
+    for (int i = 0; i < y->ndim; ++i)
+      if (residual->dims[i] != y->dims[i]) return fail(L3D_E_SHAPE, "%s: residual must have y's shape", op);
+    RowMap rm;
+    if (!make_rowmap(residual, residual->ndim - 1, &rm) || rm.nd != 1 ||
+        (n > 1 && residual->strides[residual->ndim - 1] != 1))
+      return fail(L3D_E_ALIGN, "%s: residual must be a row-major matrix", op);
+    res_ptr = elem_ptr(residual);
+    res_ld = M > 1 ? rm.strides[0] : n;
+    const int res_es = residual->dtype == L3D_F32 ? 4 : 2;
+    res_vec = (reinterpret_cast<uintptr_t>(res_ptr) % 16 == 0) && ((res_ld * res_es) % 16 == 0);
+  }
+  if (gate) {
+    if (!residual) return fail(L3D_E_SHAPE, "%s: gate needs a residual", op);
+    if (no_data(gate)) return fail(L3D_E_NULL, "%s: gate has no data", op);
+    if (gate->dtype != L3D_F32 && gate->dtype != L3D_BF16)
+      return fail(L3D_E_DTYPE, "%s: gate must be F32 or BF16", op);
+    if (numel(gate) != n || (gate->ndim >= 1 && n > 1 && gate->strides[gate->ndim - 1] != 1))
+      return fail(L3D_E_SHAPE, "%s: gate must be contiguous [n]", op);
+  }
   const size_t need = l3d_dequant_linear_workspace_size(fmt, M, n, k);
   if (!workspace || workspace_bytes < need)
     return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
@@ -805,6 +890,12 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
   p.fmt = fmt;
   p.row_bytes = (k / block_elems(fmt)) * block_bytes(fmt);
   p.bpt = 2 * block_bytes(fmt);
+  p.act = act;
+  p.res = res_ptr;
+  p.res_ld = res_ld;
+  p.res_vec = res_vec;
+  p.gate = gate ? elem_ptr(gate) : nullptr;
+  p.gate_dtype = gate ? gate->dtype : L3D_F32;
   CUtensorMap map_x, map_w, map_y;
   if (!make_map_x(&map_x, xa, uint64_t(M), uint64_t(k), uint64_t(lda)))
     return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for x", op);
@@ -865,4 +956,20 @@ extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, 
       break;
   }
   return check_launch(op);
+}
+
+extern "C" int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n,
+                                  int64_t k, const l3d_tensor* bias, const l3d_tensor* y,
+                                  void* workspace, size_t workspace_bytes, l3d_stream stream) {
+  return run_dequant_linear(x, wq, fmt, n, k, bias, ACT_NONE, nullptr, nullptr, y, workspace,
+                            workspace_bytes, stream, "l3d_dequant_linear");
+}
+
+extern "C" int l3d_dequant_linear_ex(const l3d_tensor* x, const void* wq, int fmt, int64_t n,
+                                     int64_t k, const l3d_tensor* bias, int act,
+                                     const l3d_tensor* residual, const l3d_tensor* gate,
+                                     const l3d_tensor* y, void* workspace, size_t workspace_bytes,
+                                     l3d_stream stream) {
+  return run_dequant_linear(x, wq, fmt, n, k, bias, act, residual, gate, y, workspace,
+                            workspace_bytes, stream, "l3d_dequant_linear_ex");
 }

@@ -282,6 +282,7 @@ QFMT = {"q8_0": _lib.Q8_0, "q4_0": _lib.Q4_0, "q4_k": _lib.Q4_K, "q5_k": _lib.Q5
         "q6_k": _lib.Q6_K}
 BLOCK_BYTES = {"q8_0": 34, "q4_0": 18, "q4_k": 144, "q5_k": 176, "q6_k": 210}
 BLOCK_ELEMS = {"q8_0": 32, "q4_0": 32, "q4_k": 256, "q5_k": 256, "q6_k": 256}
+ACT_CODES = {None: 0, "silu": 1, "gelu_erf": 2, "gelu": 3}
 
 
 def dequantize(wq, fmt: str, n: int, k: int, dtype=torch.float32):
@@ -309,13 +310,25 @@ class QMatMul:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.blocks.device)
         return self._ws
 
-    def forward(self, x, out_dtype=None):
-        _check_cuda(x)
+    def forward(self, x, out_dtype=None, act=None, residual=None, gate=None, out=None):
+        """y = x . deq(W)^T + bias; with `act` ("gelu", "gelu_erf", "silu") and/or
+        `residual` (+ per-column `gate`) the block's next ops run in the GEMM
+        epilogue: y = residual + gate * act(...).  `out` may be `residual`."""
+        _check_cuda(x, residual, gate, out)
         x2 = x.reshape(-1, self.k)
-        y = torch.empty((x2.shape[0], self.n), dtype=out_dtype or x.dtype, device=x.device)
+        if out is not None:
+            y = out.reshape(-1, self.n)
+        else:
+            y = torch.empty((x2.shape[0], self.n), dtype=out_dtype or x.dtype, device=x.device)
         ws = self.workspace(x2.shape[0])
-        call("l3d_dequant_linear", ref(desc(x2)), self.blocks.data_ptr(), QFMT[self.fmt], self.n,
-             self.k, ref(desc(self.bias)), ref(desc(y)), ws.data_ptr(), ws.numel(), _s(x))
+        r2 = None if residual is None else residual.reshape(-1, self.n)
+        if act is None and residual is None:
+            call("l3d_dequant_linear", ref(desc(x2)), self.blocks.data_ptr(), QFMT[self.fmt], self.n,
+                 self.k, ref(desc(self.bias)), ref(desc(y)), ws.data_ptr(), ws.numel(), _s(x))
+        else:
+            call("l3d_dequant_linear_ex", ref(desc(x2)), self.blocks.data_ptr(), QFMT[self.fmt],
+                 self.n, self.k, ref(desc(self.bias)), ACT_CODES[act], ref(desc(r2)),
+                 ref(desc(gate)), ref(desc(y)), ws.data_ptr(), ws.numel(), _s(x))
         return y.reshape(*x.shape[:-1], self.n)
 
     __call__ = forward

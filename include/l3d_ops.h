@@ -290,6 +290,20 @@ int l3d_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n, 
                        const l3d_tensor* bias, const l3d_tensor* y, void* workspace,
                        size_t workspace_bytes, l3d_stream stream);
 
+/* As l3d_dequant_linear, with the element-wise ops that follow the linear in
+ * the reference's blocks fused into the GEMM epilogue (no extra pass over y):
+ *   y = residual + gate * act(x . deq(W)^T + bias)
+ * act: 0 none, 1 SiLU, 2 GELU-erf, 3 GELU-tanh (computed in f32 before the
+ * single rounding to y's dtype); residual: y's dtype and shape, row-major, or
+ * NULL (it may be y itself, for an in-place x += ...; y must not overlap x);
+ * gate: [N] F32/BF16, or NULL for 1 (only with a residual).  Replaces
+ * Trellis2FeedForward's mlp.0 + gelu (crate/runtime/trellis2_blocks.rs:
+ * 558-561) and the gated residuals xs + gate * h (:632-633, :644-645). */
+int l3d_dequant_linear_ex(const l3d_tensor* x, const void* wq, int fmt, int64_t n, int64_t k,
+                          const l3d_tensor* bias, int act, const l3d_tensor* residual,
+                          const l3d_tensor* gate, const l3d_tensor* y, void* workspace,
+                          size_t workspace_bytes, l3d_stream stream);
+
 /* ---- GGUF tensor index (the on-disk format feeding a13) ------------------------ */
 
 /* One tensor of a GGUF file.  name points into the caller's buffer (not

@@ -133,3 +133,65 @@ def test_dequant_linear_kquants(ops, orc, dev, M, N, K, fmt):
     bound = 2e-5 * (np.abs(xv) @ np.abs(wb).T) + 1e-6
     err = np.abs(y - ref)
     assert np.all(err <= bound), f"max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"
+
+
+def _act_ref(name, z):
+    from math import sqrt
+
+    from scipy.special import erf
+
+    if name == "gelu":
+        return 0.5 * z * (1.0 + np.tanh(sqrt(2.0 / np.pi) * (z + 0.044715 * z ** 3)))
+    if name == "gelu_erf":
+        return 0.5 * z * (1.0 + erf(z / sqrt(2.0)))
+    if name == "silu":
+        return z / (1.0 + np.exp(-z))
+    return z
+
+
+@pytest.mark.parametrize("M,N,K,act,res,gate,ydt", [
+    (700, 1024, 1536, "gelu", False, False, "bf16"),       # mlp.0 + GELU-tanh, TMA-store epilogue
+    (64, 512, 512, "gelu", False, False, "bf16"),          # small M: fused-decode mode, direct stores
+    (600, 768, 512, "gelu_erf", False, False, "f32"),      # accurate activation for f32 output
+    (700, 1536, 1024, None, True, True, "bf16"),           # x += gate * linear(h), in place
+    (300, 300, 256, "silu", True, False, "f32"),           # N tail, residual without gate
+    (37, 520, 1024, None, True, True, "bf16"),             # small M, N tail, gated residual
+])
+def test_dequant_linear_fused_epilogue(ops, orc, dev, M, N, K, act, res, gate, ydt):
+    """y = residual + gate * act(x . W^T + b) against the f64 product of the same
+    bf16 operands; bounds: the GEMM's f32 accumulation (scaled by the largest
+    derivative of the activation, < 1.13), one rounding to bf16, and the
+    tanh.approx / ex2.approx forms used for 16-bit outputs (abs. error below
+    3e-4 |z|)."""
+    import torch
+
+    x, q, b = _case(orc, M, N, K, "q8_0", 90 + M)
+    r = rng(91 + M)
+    xb = torch.from_numpy(x).to(dev).to(torch.bfloat16)
+    xv = xb.float().cpu().numpy().astype(np.float64)
+    wb = orc.round_bf16(orc.dequantize(q, "q8_0", N, K)).astype(np.float64)
+    tdt = torch.float32 if ydt == "f32" else torch.bfloat16
+    mm = ops.QMatMul(torch.from_numpy(q).to(dev), "q8_0", N, K, bias=torch.from_numpy(b).to(dev))
+    z = xv @ wb.T + b
+    bound = 1.2 * (2e-5 * (np.abs(xv) @ np.abs(wb).T)) + 1e-6
+    ref = _act_ref(act, z)
+    kw = {"act": act}
+    if res:
+        r0 = torch.from_numpy(r.standard_normal((M, N)).astype(np.float32)).to(dev).to(tdt)
+        g = torch.from_numpy((0.5 + r.random(N)).astype(np.float32)).to(dev) if gate else None
+        rv = r0.float().cpu().numpy().astype(np.float64)
+        gv = g.cpu().numpy().astype(np.float64) if gate else 1.0
+        ref = rv + gv * ref
+        bound = bound * (np.max(np.abs(gv)) if gate else 1.0)
+        kw.update(residual=r0, gate=g, out=r0)  # in place: x += gate * ...
+    y = mm(xb, out_dtype=tdt, **kw)
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    if ydt == "bf16":
+        bound = bound + np.abs(ref) * 2.0 ** -8 + (3e-4 * np.abs(z) if act else 0.0)
+    else:
+        bound = bound + 1e-6 * np.abs(ref)
+    err = np.abs(got - ref)
+    assert np.all(err <= bound), f"max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"
+    if res:
+        assert y.data_ptr() == r0.data_ptr()

@@ -50,15 +50,25 @@ constexpr int EPI_COLS = 64;
 constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 4;  // 8 KB
 constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
-// Operand-B modes.  MODE_RAW_TMA / MODE_RAW_LDG decode GGML blocks in the
+// Operand modes.  MODE_RAW_TMA / MODE_RAW_LDG decode GGML blocks in the
 // prologue (3 stages of x + B + raw window); MODE_BF16 streams a bf16 copy of
 // the decoded weights with TMA (4 stages of x + B), used when the M dimension
 // is large enough that decoding per 128-row tile would repeat the work
-// hundreds of times.
-enum { MODE_RAW_TMA = 0, MODE_RAW_LDG = 1, MODE_BF16 = 2 };
+// hundreds of times.  MODE_GATHER is the submanifold sparse conv: the worker
+// warps gather the A tile (the 27 neighbour rows of each output row, one
+// kernel offset per Cin-wide stretch of K) and TMA streams the bf16
+// [27, Cout, Cin] weights.
+// MODE_PAIRS is the same conv one kernel offset at a time over its compacted
+// neighbour pairs: rows are gathered through the pair sources and the
+// epilogue adds the product into the pair destinations of an f32
+// accumulator (launched once per offset, in ascending order).
+enum { MODE_RAW_TMA = 0, MODE_RAW_LDG = 1, MODE_BF16 = 2, MODE_GATHER = 3, MODE_PAIRS = 4 };
 template <int MODE>
 struct ModeCfg {
-  static constexpr bool FUSED = MODE != MODE_BF16;
+  static constexpr bool FUSED = MODE == MODE_RAW_TMA || MODE == MODE_RAW_LDG;  // decode W
+  static constexpr bool PAIRS = MODE == MODE_PAIRS;
+  static constexpr bool GATHER = MODE == MODE_GATHER || PAIRS;                 // gather A
+  static constexpr bool WORKERS = FUSED || GATHER;  // warps 6.. build an operand
   static constexpr int NST = FUSED ? 3 : 4;
   static constexpr int RAW = FUSED ? RAW_BYTES : 0;
   static constexpr int EPI = FUSED ? 0 : EPI_BYTES;  // fused modes store directly
@@ -153,6 +163,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 
 // K-major, 128B-swizzled operand tile: rows of 128 B, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
@@ -223,6 +241,9 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
@@ -259,26 +280,62 @@ struct Params {
   int fmt;
   int bpt;            // raw bytes per 64-wide K step (2 blocks)
   int tma_store;      // epilogue writes y through the map_y tensor map
+  int y_vec;          // y's base and row stride are 16-byte aligned (vector stores)
+  int bias_vec;       // bias is 16-byte aligned (vector loads)
   // Fused epilogue: y = res + gate * act(acc + bias).
   int act;            // Act code (0: none)
   const void* res;    // [M, N] rows of res_ld elements, y's dtype; null: none
   int64_t res_ld;
   int res_vec;        // res rows are 16-byte aligned (vector loads)
+  int res_tma;        // TMA-store epilogue: res tiles arrive by TMA (map_r)
   const void* gate;   // [N] or null (= 1)
   int gate_dtype;
+  // Sparse conv (MODE_GATHER): A[m, k * cin_pad + c] = feats[nbr[m, k], c]
+  // (0 for nbr < 0 or c >= cin).
+  const int32_t* nbr;              // [M, 27]
+  const __nv_bfloat16* feats;      // rows of feats_ld elements
+  int64_t feats_ld;
+  int cin, cin_pad;                // cin_pad = cin rounded up to BK
+  // MODE_PAIRS: rows m < *pcount: A[m] = feats[psrc[m]], y[pdst[m]] += acc[m]
+  // (f32 y); the weights of offset koff.
+  const int32_t* psrc;
+  const int32_t* pdst;
+  const int32_t* pcount;
+  int koff;
 };
 
 // The fused epilogue ops on NC consecutive columns [col0, col0 + NC) of one
 // row, after the bias: the activation (the reduced-cost forms for 16-bit
 // outputs), then the gated residual, 8 columns at a time.  Columns past N are
 // left alone.
+template <int A, bool FAST, int NC>
+__device__ __forceinline__ void act_chunk(float (&v)[NC]) {
+#pragma unroll
+  for (int i = 0; i < NC; ++i) v[i] = act_t<A, FAST>(v[i]);
+}
+// One dispatch per chunk, so each variant's loop is contiguous code.
+template <int NC>
+__device__ __forceinline__ void epi_act(int act, bool fast, float (&v)[NC]) {
+  if (fast) {
+    switch (act) {
+      case ACT_SILU: act_chunk<ACT_SILU, true>(v); break;
+      case ACT_GELU_ERF: act_chunk<ACT_GELU_ERF, true>(v); break;
+      case ACT_GELU_TANH: act_chunk<ACT_GELU_TANH, true>(v); break;
+      default: break;
+    }
+  } else {
+    switch (act) {
+      case ACT_SILU: act_chunk<ACT_SILU, false>(v); break;
+      case ACT_GELU_ERF: act_chunk<ACT_GELU_ERF, false>(v); break;
+      case ACT_GELU_TANH: act_chunk<ACT_GELU_TANH, false>(v); break;
+      default: break;
+    }
+  }
+}
+
 template <int NC>
 __device__ __forceinline__ void epi_post(const Params& p, int row, int col0, float (&v)[NC]) {
-  if (p.act) {
-    const bool fast = p.y_dtype != L3D_F32;
-#pragma unroll
-    for (int i = 0; i < NC; ++i) v[i] = fast ? act_dyn_fast(p.act, v[i]) : act_dyn(p.act, v[i]);
-  }
+  if (p.act) epi_act<NC>(p.act, p.y_dtype != L3D_F32, v);
   if (!p.res || row >= p.M) return;
   const bool bf = p.y_dtype == L3D_BF16;
   const char* rrow = static_cast<const char*>(p.res) + (int64_t(row) * p.res_ld + col0) * (bf ? 2 : 4);
@@ -391,12 +448,51 @@ __device__ __forceinline__ void dequant_tile(const Params& p, const uint8_t* raw
   }
 }
 
+// Gather the 128 x 64 A tile of (m0, kb) into the K-major SW128 layout (row r
+// at r * 128 bytes, its 16-byte chunk j at chunk j ^ (r % 8)).  256 threads,
+// 4 chunks each: thread t takes chunk t % 8 of rows t / 8 + 32 i; src[] holds
+// the rows' neighbours for the current kernel offset and is reloaded only
+// when the offset changes.
+template <bool PAIRS>
+__device__ __forceinline__ void gather_tile(const Params& p, uint8_t* tile, int m0, int kb, int t,
+                                            int rows, int& cur_off, int32_t (&src)[4]) {
+  const int kk = kb * BK;
+  const int off = PAIRS ? 0 : kk / p.cin_pad, c0 = kk - off * p.cin_pad;
+  if (off != cur_off) {
+    cur_off = off;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = m0 + (t >> 3) + 32 * i;
+      if constexpr (PAIRS) src[i] = row < rows ? __ldg(p.psrc + row) : -1;
+      else src[i] = row < rows ? __ldg(p.nbr + int64_t(row) * 27 + off) : -1;
+    }
+  }
+  const int j = t & 7;
+  const int c = c0 + 8 * j;
+  uint4 v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (src[i] >= 0 && c < p.cin)
+      v[i] = __ldg(reinterpret_cast<const uint4*>(p.feats + int64_t(src[i]) * p.feats_ld + c));
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (t >> 3) + 32 * i;
+    *reinterpret_cast<uint4*>(tile + r * 128 + ((j ^ (r & 7)) << 4)) = v[i];
+  }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                 const __grid_constant__ CUtensorMap map_y, const Params p) {
+                 const __grid_constant__ CUtensorMap map_y, const __grid_constant__ CUtensorMap map_r,
+                 const Params p) {
   constexpr bool RAW_TMA = MODE == MODE_RAW_TMA;
   constexpr bool FUSED = ModeCfg<MODE>::FUSED;
+  constexpr bool GATHER = ModeCfg<MODE>::GATHER;
+  constexpr bool PAIRS = ModeCfg<MODE>::PAIRS;
+  constexpr bool WORKERS = ModeCfg<MODE>::WORKERS;
   constexpr int STAGES = ModeCfg<MODE>::NST;
   constexpr int RAWB = ModeCfg<MODE>::RAW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -414,9 +510,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* tempty = bars + 3 * STAGES + 2;        // [2] epilogue -> MMA
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+  uint64_t* rbars = bars + 3 * STAGES + 7;         // [4][2] residual TMA -> epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  // Rows of the output (MODE_PAIRS: this offset's pair count, on the device).
+  int rows_m = p.M;
+  if constexpr (PAIRS) rows_m = min(__ldg(p.pcount), p.M);
+  const int num_m = (rows_m + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
   const int tiles = num_m * num_n;
   const int kblocks = (p.K + BK - 1) / BK;
 
@@ -430,6 +530,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
+    for (int w = 0; w < 8; ++w) mbar_init(&rbars[w], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -455,8 +556,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
           mbar_expect_tx(&lfull[stage], MODE == MODE_RAW_TMA ? A_BYTES + RAW_BYTES
                                         : MODE == MODE_BF16  ? A_BYTES + B_BYTES
+                                        : GATHER             ? B_BYTES  // gather / pairs
                                                              : A_BYTES);
-          tma_load_2d(sa + stage * A_BYTES, &map_x, &lfull[stage], kb * BK, m0);
+          if constexpr (GATHER) {
+            // Weights [27, Cout, Cin]: box of 64 channels x 256 outputs of one offset.
+            const int kk = kb * BK, off = PAIRS ? 0 : kk / p.cin_pad;
+            tma_load_3d(sb + stage * B_BYTES, &map_w, &lfull[stage], kk - off * p.cin_pad, n0,
+                        PAIRS ? p.koff : off);
+          } else {
+            tma_load_2d(sa + stage * A_BYTES, &map_x, &lfull[stage], kb * BK, m0);
+          }
           if constexpr (RAW_TMA) {
             // 16-byte aligned window (in 2-byte elements) holding this K step.
             const int c0 = ((kb * p.bpt) >> 4) << 3;
@@ -484,7 +593,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW) ||
-              (FUSED && !mbar_wait(&bfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_FULL))) {
+              (WORKERS && !mbar_wait(&bfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_FULL))) {
             ok = false;
             break;
           }
@@ -507,35 +616,70 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
+    // TMA-store epilogue staging, 8 KB per epilogue warp.  Without a residual,
+    // bf16 chunks (32 x 64 = 4 KB) alternate between its two halves (a store
+    // can still be reading one while the next chunk is written) and f32
+    // chunks use all of it.  With a residual, bf16: the first half receives
+    // the residual chunks by TMA and the second half stages the output, so
+    // the next residual load starts as soon as the current one is consumed;
+    // f32: the residual chunk arrives in the staging and is updated in place.
+    const bool f32o = p.y_dtype == L3D_F32;
+    uint8_t* stg = se + (warp - 2) * EPI_WARP_BYTES;
+    uint64_t* rbar = &rbars[(warp - 2) * 2];
+    uint32_t rph = 0;  // parity of this warp's residual barrier
+    int last_b = -1;   // staging half of the most recent store (bf16, no residual)
+    // Residual chunk ci (64 columns) of the tile at (m0, n0) by TMA into stg.
+    auto issue_res = [&](int m0, int n0, int ci) {
+      const int col0 = n0 + ci * EPI_COLS;
+      if (col0 >= p.N) return;
+      // The warp's generic reads of the staging come before the async write.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      const bool two = f32o && col0 + 32 < p.N;
+      mbar_expect_tx(rbar, two ? 8192u : 4096u);
+      tma_load_2d(stg, &map_r, rbar, col0, m0 + quarter * 32);
+      if (two) tma_load_2d(stg + 4096, &map_r, rbar, col0 + 32, m0 + quarter * 32);
+    };
     for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++local) {
       const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      if constexpr (!FUSED) {
+        // The tile's first residual chunk loads while the MMA still works.
+        if (p.tma_store && p.res && p.res_tma && lane == 0) {
+          if (f32o) bulk_wait_read0();  // in-place staging: the last store has read it
+          issue_res(m0, n0, 0);
+        }
+      }
       if (!mbar_wait_idle(&tfull[acc], acc_phase, abort_flag, p.status, ST_TIMEOUT_TMEM)) break;
       tc_fence_after();
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
       if constexpr (!FUSED) if (p.tma_store) {
-        // 32 rows x 64 columns per step: TMEM -> registers (+ bias) -> this
-        // warp's staging (128B-swizzled boxes of 128 bytes per row) -> TMA
-        // stores of whole 128-byte lines; rows / columns past the matrix are
-        // clipped by the tensor map.
-        uint8_t* stg = se + (warp - 2) * EPI_WARP_BYTES;
-        const bool f32 = p.y_dtype == L3D_F32;
+        // 32 rows x 64 columns per step: TMEM -> registers (+ bias, act,
+        // residual) -> staging (128B-swizzled boxes of 128 bytes per row) ->
+        // TMA stores of whole 128-byte lines; rows / columns past the matrix
+        // are clipped by the tensor maps.
+        const bool f32 = f32o;
+        const bool tres = p.res && p.res_tma;
+        bool eok = true;
 #pragma unroll 1
         for (int c = 0; c < BN; c += EPI_COLS) {
+          const int col0 = n0 + c;
+          if (col0 >= p.N) break;  // warp-uniform; later chunks are past N too
+          const int ci = c / EPI_COLS;
+          // Output staging of this chunk.
+          const int b = tres ? 1 : (f32 ? 0 : (ci & 1));
+          uint8_t* obuf = f32 ? stg : stg + b * 4096;
           float v[EPI_COLS];
           {
-            float a[32], b[32];
+            float a[32], b2[32];
             tmem_ld32(taddr + uint32_t(c), a);
-            tmem_ld32(taddr + uint32_t(c + 32), b);
+            tmem_ld32(taddr + uint32_t(c + 32), b2);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = b[i]; }
+            for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = b2[i]; }
           }
-          const int col0 = n0 + c;
-          if (col0 >= p.N) continue;  // warp-uniform
           if (p.bias) {
-            if (col0 + EPI_COLS <= p.N && p.bias_dtype == L3D_F32) {
+            if (col0 + EPI_COLS <= p.N && p.bias_dtype == L3D_F32 && p.bias_vec) {
               const float4* b4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col0);
 #pragma unroll
               for (int q = 0; q < EPI_COLS / 4; ++q) {
@@ -552,13 +696,77 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
-          if (p.act || p.res) epi_post<EPI_COLS>(p, row, col0, v);
-          // The previous stores from this staging area must have read it.
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
+          if (tres) {
+            if (p.act) {
+              // In two halves of 32 columns (fewer live temporaries).
+              epi_act<32>(p.act, !f32, *reinterpret_cast<float(*)[32]>(&v[0]));
+              epi_act<32>(p.act, !f32, *reinterpret_cast<float(*)[32]>(&v[32]));
+            }
+          } else if (p.act || p.res) {
+            epi_post<32>(p, row, col0, *reinterpret_cast<float(*)[32]>(&v[0]));
+            epi_post<32>(p, row, col0 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+          }
           // Row `lane` of a box is 128 bytes = 8 chunks of 16 B; chunk j lives
-          // at chunk j ^ (lane % 8) (the SWIZZLE_128B pattern of the map).
-          uint8_t* rowp = stg + lane * 128;
+          // at chunk j ^ (lane % 8) (the SWIZZLE_128B pattern of the maps).
+          if (tres) {
+            if (!mbar_wait(rbar, rph, abort_flag, p.status, ST_TIMEOUT_RAW)) {
+              eok = false;
+              break;
+            }
+            rph ^= 1u;
+            // y = r + g * v, with r read from the staged residual chunk.
+            const uint8_t* rrow = stg + lane * 128;
+            auto gate_at = [&](int i) {
+              if (!p.gate) return 1.f;
+              const int col = col0 + i < p.N ? col0 + i : p.N - 1;
+              return p.gate_dtype == L3D_F32
+                         ? __ldg(static_cast<const float*>(p.gate) + col)
+                         : __bfloat162float(static_cast<const __nv_bfloat16*>(p.gate)[col]);
+            };
+            if (f32) {
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                const int bx = q >> 3, j = q & 7;
+                const float4 r = *reinterpret_cast<const float4*>(rrow + bx * 4096 + ((j ^ (lane & 7)) << 4));
+                v[4 * q] = fmaf(gate_at(4 * q), v[4 * q], r.x);
+                v[4 * q + 1] = fmaf(gate_at(4 * q + 1), v[4 * q + 1], r.y);
+                v[4 * q + 2] = fmaf(gate_at(4 * q + 2), v[4 * q + 2], r.z);
+                v[4 * q + 3] = fmaf(gate_at(4 * q + 3), v[4 * q + 3], r.w);
+              }
+            } else {
+              const bool gvec = p.gate && p.gate_dtype == L3D_F32 && col0 + EPI_COLS <= p.N &&
+                                (reinterpret_cast<uintptr_t>(p.gate) & 15) == 0;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float r[8], g[8];
+                unpack(*reinterpret_cast<const uint4*>(rrow + ((j ^ (lane & 7)) << 4)), r,
+                       __nv_bfloat16());
+                if (gvec) {
+                  const float4* g4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.gate) + col0 + 8 * j);
+                  const float4 ga = __ldg(g4), gb = __ldg(g4 + 1);
+                  g[0] = ga.x; g[1] = ga.y; g[2] = ga.z; g[3] = ga.w;
+                  g[4] = gb.x; g[5] = gb.y; g[6] = gb.z; g[7] = gb.w;
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) g[e] = gate_at(8 * j + e);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[8 * j + e] = fmaf(g[e], v[8 * j + e], r[e]);
+              }
+              // Every lane has read the residual half: load the next chunk.
+              __syncwarp();
+              if (lane == 0 && ci + 1 < BN / EPI_COLS) issue_res(m0, n0, ci + 1);
+            }
+          }
+          if (lane == 0) {
+            // The store that last read this staging has finished reading it
+            // (bf16 without residual: the newest store may still be reading
+            // the other half).
+            if (!tres && !f32 && last_b != b) bulk_wait_read1();
+            else if (!(tres && f32)) bulk_wait_read0();
+          }
+          __syncwarp();
+          uint8_t* rowp = obuf + lane * 128;
           if (f32) {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {  // two boxes of 32 columns
@@ -578,11 +786,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&map_y, stg, col0, m0 + quarter * 32);
-            if (f32 && col0 + 32 < p.N) tma_store_2d(&map_y, stg + 4096, col0 + 32, m0 + quarter * 32);
+            tma_store_2d(&map_y, obuf, col0, m0 + quarter * 32);
+            if (f32 && col0 + 32 < p.N) tma_store_2d(&map_y, obuf + 4096, col0 + 32, m0 + quarter * 32);
             bulk_commit();
+            if (tres && f32 && ci + 1 < BN / EPI_COLS) {
+              bulk_wait_read0();  // in place: this store has read the staging
+              issue_res(m0, n0, ci + 1);
+            }
           }
+          last_b = b;
         }
+        if (!eok) break;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -593,7 +807,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         float v[32];
         tmem_ld32(taddr + uint32_t(c), v);
         const int col0 = n0 + c;
-        if (row < p.M && col0 < p.N) {
+        if (row < rows_m && col0 < p.N) {
+          if constexpr (PAIRS) {
+            // y[pdst[row]] += acc (f32 accumulator; rows are distinct per offset).
+            float* yr = static_cast<float*>(p.y) + int64_t(__ldg(p.pdst + row)) * p.y_ld + col0;
+            if (col0 + 32 <= p.N && p.y_vec) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 a = *reinterpret_cast<const float4*>(yr + q * 4);
+                a.x += v[q * 4]; a.y += v[q * 4 + 1]; a.z += v[q * 4 + 2]; a.w += v[q * 4 + 3];
+                *reinterpret_cast<float4*>(yr + q * 4) = a;
+              }
+            } else {
+              for (int i = 0; i < 32 && col0 + i < p.N; ++i) yr[i] += v[i];
+            }
+            continue;
+          }
           if (p.bias) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -607,7 +836,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (p.act || p.res) epi_post<32>(p, row, col0, v);
           if (p.y_dtype == L3D_BF16) {
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + int64_t(row) * p.y_ld + col0;
-            if (col0 + 32 <= p.N) {
+            if (col0 + 32 <= p.N && p.y_vec) {
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 float f[8];
@@ -620,7 +849,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           } else {
             float* yr = static_cast<float*>(p.y) + int64_t(row) * p.y_ld + col0;
-            if (col0 + 32 <= p.N) {
+            if (col0 + 32 <= p.N && p.y_vec) {
 #pragma unroll
               for (int q = 0; q < 8; ++q)
                 *reinterpret_cast<float4*>(yr + q * 4) =
@@ -636,22 +865,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
     if (p.tma_store && lane == 0) bulk_wait0();  // stores complete before teardown
-  } else if constexpr (FUSED) {
-    // --------------------------------------------------------- dequantisers
+  } else if constexpr (WORKERS) {
+    // ------------------------------------- dequantisers / neighbour gatherers
     const int t = threadIdx.x - 6 * 32;  // 0 .. 255
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-      const int n0 = (tile % num_n) * BN;
+      const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+      int cur_off = -1;
+      int32_t src[4];
       bool ok = true;
       for (int kb = 0; kb < kblocks; ++kb) {
-        // The raw window (and the x tile) of this stage have landed, which also
-        // means the MMA has released the stage's B buffer.
+        // The stage's TMA loads have landed, which also means the MMA has
+        // released the stage's buffers.
         if (!mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW)) {
           ok = false;
           break;
         }
-        dequant_tile<RAW_TMA>(p, sr + stage * RAWB, sb + stage * B_BYTES, n0, kb, t);
+        if constexpr (GATHER) {
+          gather_tile<PAIRS>(p, sa + stage * A_BYTES, m0, kb, t, rows_m, cur_off, src);
+        } else {
+          (void)m0;
+          dequant_tile<RAW_TMA>(p, sr + stage * RAWB, sb + stage * B_BYTES, n0, kb, t);
+        }
         // Generic-proxy smem writes must be visible to the tensor core.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -744,6 +980,21 @@ static bool make_map_w(CUtensorMap* m, const void* base, uint64_t n, uint64_t ro
   const cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Sparse-conv weights [27, cout, cin] bf16 (contiguous): box 64 channels x 256
+// outputs x 1 offset, 128B swizzle; channels past cin / outputs past cout read
+// as zero.
+static bool make_map_w27(CUtensorMap* m, const void* base, uint64_t cout, uint64_t cin) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {cin, cout, 27};
+  const cuuint64_t strides[2] = {cin * 2, cout * cin * 2};
+  const cuuint32_t box[3] = {uint32_t(BK), uint32_t(BN), 1u};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -885,6 +1136,9 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
   p.y = const_cast<char*>(elem_ptr(y));
   p.y_ld = y_ld;
   p.y_dtype = y->dtype;
+  p.y_vec = (reinterpret_cast<uintptr_t>(p.y) % 16 == 0) &&
+            ((y_ld * (y->dtype == L3D_F32 ? 4 : 2)) % 16 == 0);
+  p.bias_vec = bias ? (reinterpret_cast<uintptr_t>(elem_ptr(bias)) % 16 == 0) : 0;
   p.status = status;
   p.wq = static_cast<const uint8_t*>(wq);
   p.fmt = fmt;
@@ -925,6 +1179,14 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
     mode = raw_tma ? MODE_RAW_TMA : MODE_RAW_LDG;
     p.tma_store = 0;  // no shared memory left for staging: direct stores
   }
+  // Residual tiles by TMA (into the store staging) when the epilogue stores by
+  // TMA and the residual rows are 16-byte aligned; otherwise direct loads.
+  CUtensorMap map_r = map_y;  // unused unless res_tma
+  p.res_tma = (p.tma_store && res_ptr && res_vec &&
+               make_map_y(&map_r, const_cast<void*>(res_ptr), y->dtype, uint64_t(M), uint64_t(n),
+                          uint64_t(res_ld)))
+                  ? 1
+                  : 0;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -946,13 +1208,13 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
   const int grid = tiles < sm_count() ? tiles : sm_count();
   switch (mode) {
     case MODE_RAW_TMA:
-      qgemm_kernel<MODE_RAW_TMA><<<grid, THREADS, ModeCfg<MODE_RAW_TMA>::SMEM, s>>>(map_x, map_w, map_y, p);
+      qgemm_kernel<MODE_RAW_TMA><<<grid, THREADS, ModeCfg<MODE_RAW_TMA>::SMEM, s>>>(map_x, map_w, map_y, map_r, p);
       break;
     case MODE_RAW_LDG:
-      qgemm_kernel<MODE_RAW_LDG><<<grid, THREADS, ModeCfg<MODE_RAW_LDG>::SMEM, s>>>(map_x, map_w, map_y, p);
+      qgemm_kernel<MODE_RAW_LDG><<<grid, THREADS, ModeCfg<MODE_RAW_LDG>::SMEM, s>>>(map_x, map_w, map_y, map_r, p);
       break;
     default:
-      qgemm_kernel<MODE_BF16><<<grid, THREADS, ModeCfg<MODE_BF16>::SMEM, s>>>(map_x, map_w, map_y, p);
+      qgemm_kernel<MODE_BF16><<<grid, THREADS, ModeCfg<MODE_BF16>::SMEM, s>>>(map_x, map_w, map_y, map_r, p);
       break;
   }
   return check_launch(op);
@@ -972,4 +1234,284 @@ extern "C" int l3d_dequant_linear_ex(const l3d_tensor* x, const void* wq, int fm
                                      l3d_stream stream) {
   return run_dequant_linear(x, wq, fmt, n, k, bias, act, residual, gate, y, workspace,
                             workspace_bytes, stream, "l3d_dequant_linear_ex");
+}
+
+// ------------------------------------------------------------- sparse conv
+// Workspace: [0, 256) status word, then room for a contiguous bf16 copy of
+// feats (used when they are F32 or their rows are not 16-byte aligned).
+extern "C" size_t l3d_sparse_conv3d_workspace_size(int64_t n, int64_t cin, int feats_dtype) {
+  (void)feats_dtype;
+  if (n < 0 || cin < 0) return 0;
+  return 256 + align256(size_t(n) * size_t(cin) * 2);
+}
+
+extern "C" int l3d_sparse_conv3d(const l3d_tensor* feats, const l3d_tensor* nbr,
+                                 const l3d_tensor* weight, const l3d_tensor* bias,
+                                 const l3d_tensor* out, void* workspace, size_t workspace_bytes,
+                                 l3d_stream stream) {
+  const char* op = "l3d_sparse_conv3d";
+  using namespace l3d::gemm;
+  if (!feats || !nbr || !weight || !out) return fail(L3D_E_NULL, "%s: feats, nbr, weight, out required", op);
+  if (feats->dtype != L3D_BF16 && feats->dtype != L3D_F32)
+    return fail(L3D_E_DTYPE, "%s: feats must be BF16 or F32", op);
+  if (weight->dtype != L3D_BF16) return fail(L3D_E_DTYPE, "%s: weight must be BF16 [27, Cout, Cin]", op);
+  if (nbr->dtype != L3D_I32) return fail(L3D_E_DTYPE, "%s: nbr must be I32", op);
+  if (out->dtype != L3D_BF16 && out->dtype != L3D_F32)
+    return fail(L3D_E_DTYPE, "%s: out must be BF16 or F32", op);
+  if (feats->ndim != 2 || weight->ndim != 3 || weight->dims[0] != 27 || nbr->ndim != 2 ||
+      out->ndim != 2)
+    return fail(L3D_E_SHAPE, "%s: feats [N, Cin], nbr [N, 27], weight [27, Cout, Cin], out [N, Cout]", op);
+  const int64_t n = feats->dims[0], cin = feats->dims[1], cout = weight->dims[1];
+  if (weight->dims[2] != cin || nbr->dims[0] != n || nbr->dims[1] != 27 || out->dims[0] != n ||
+      out->dims[1] != cout)
+    return fail(L3D_E_SHAPE, "%s: shapes do not agree", op);
+  if (cin <= 0 || cin % 8 || cout <= 0)
+    return fail(L3D_E_UNSUPPORTED, "%s: Cin must be a positive multiple of 8", op);
+  if (n > INT32_MAX || cout > INT32_MAX || 27 * ((cin + BK - 1) / BK * BK) > INT32_MAX)
+    return fail(L3D_E_UNSUPPORTED, "%s: dimensions exceed 2^31", op);
+  if (bias) {
+    if (no_data(bias)) return fail(L3D_E_NULL, "%s: bias has no data", op);
+    if (bias->dtype != L3D_F32 && bias->dtype != L3D_BF16)
+      return fail(L3D_E_DTYPE, "%s: bias must be F32 or BF16", op);
+    if (numel(bias) != cout || (bias->ndim >= 1 && cout > 1 && bias->strides[bias->ndim - 1] != 1))
+      return fail(L3D_E_SHAPE, "%s: bias must be contiguous [Cout]", op);
+  }
+  const size_t need = l3d_sparse_conv3d_workspace_size(n, cin, feats->dtype);
+  if (!workspace || workspace_bytes < need)
+    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(L3D_E_ALIGN, "%s: workspace must be 256-byte aligned", op);
+  if (n == 0) return L3D_OK;
+  if (no_data(feats) || no_data(nbr) || no_data(weight) || no_data(out))
+    return fail(L3D_E_NULL, "%s: null data pointer", op);
+  if ((cin > 1 && feats->strides[1] != 1) || (cout > 1 && out->strides[1] != 1) ||
+      nbr->strides[1] != 1 || (n > 1 && nbr->strides[0] != 27))
+    return fail(L3D_E_ALIGN, "%s: feats/out rows and nbr must be contiguous", op);
+  if (weight->strides[2] != 1 || weight->strides[1] != cin || weight->strides[0] != cout * cin)
+    return fail(L3D_E_ALIGN, "%s: weight must be contiguous [27, Cout, Cin]", op);
+  const void* wp = elem_ptr(weight);
+  if (reinterpret_cast<uintptr_t>(wp) % 16) return fail(L3D_E_ALIGN, "%s: weight must be 16-byte aligned", op);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  if (cudaMemsetAsync(status, 0, 256, s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: status clear failed", op);
+  // feats as bf16 rows with a 16-byte aligned stride.
+  const void* fa = elem_ptr(feats);
+  int64_t fld = n > 1 ? feats->strides[0] : cin;
+  if (feats->dtype == L3D_F32 || (fld * 2) % 16 || reinterpret_cast<uintptr_t>(fa) % 16) {
+    __nv_bfloat16* fb = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+    if (feats->dtype == L3D_F32) {
+      int64_t blocks = (n * cin + 255) / 256;
+      if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
+      f32_to_bf16_kernel<<<int(blocks), 256, 0, s>>>(static_cast<const float*>(fa), fld, n, cin, fb);
+    } else if (cudaMemcpy2DAsync(fb, size_t(cin) * 2, fa, size_t(fld) * 2, size_t(cin) * 2, size_t(n),
+                                 cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+      return fail(L3D_E_CUDA, "%s: feats copy failed", op);
+    }
+    fa = fb;
+    fld = cin;
+  }
+  Params p{};
+  p.M = int(n);
+  p.N = int(cout);
+  p.cin = int(cin);
+  p.cin_pad = int((cin + BK - 1) / BK * BK);
+  p.K = 27 * p.cin_pad;
+  p.bias = bias ? elem_ptr(bias) : nullptr;
+  p.bias_dtype = bias ? bias->dtype : L3D_F32;
+  p.y = const_cast<char*>(elem_ptr(out));
+  p.y_ld = n > 1 ? out->strides[0] : cout;
+  p.y_dtype = out->dtype;
+  p.y_vec = (reinterpret_cast<uintptr_t>(p.y) % 16 == 0) &&
+            ((p.y_ld * (out->dtype == L3D_F32 ? 4 : 2)) % 16 == 0);
+  p.bias_vec = bias ? (reinterpret_cast<uintptr_t>(elem_ptr(bias)) % 16 == 0) : 0;
+  p.status = status;
+  p.nbr = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(nbr)));
+  p.feats = static_cast<const __nv_bfloat16*>(fa);
+  p.feats_ld = fld;
+  CUtensorMap map_w, map_y;
+  if (!make_map_w27(&map_w, wp, uint64_t(cout), uint64_t(cin)))
+    return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
+  const int yes = out->dtype == L3D_F32 ? 4 : 2;
+  p.tma_store = (reinterpret_cast<uintptr_t>(p.y) % 16 == 0) && ((p.y_ld * yes) % 16 == 0) &&
+                        make_map_y(&map_y, p.y, out->dtype, uint64_t(n), uint64_t(cout), uint64_t(p.y_ld))
+                    ? 1
+                    : 0;
+  if (!p.tma_store) map_y = map_w;  // unused
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_GATHER>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ModeCfg<MODE_GATHER>::SMEM);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
+  const int tiles = int(((n + BM - 1) / BM) * ((cout + BN - 1) / BN));
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  qgemm_kernel<MODE_GATHER><<<grid, THREADS, ModeCfg<MODE_GATHER>::SMEM, s>>>(map_w, map_w, map_y, map_w, p);
+  return check_launch(op);
+}
+
+// ------------------------------------------------- sparse conv over pair lists
+// acc [n, cout] f32 rows of ld elements -> out = acc + bias (out's dtype).
+__global__ void conv_finish_kernel(const float* __restrict__ acc, int64_t ald, int64_t n,
+                                   int64_t cout, const void* bias, int bias_dtype, void* out,
+                                   int64_t old_, int out_dtype) {
+  const int64_t total = n * cout;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cout, c = i - r * cout;
+    float v = acc[r * ald + c];
+    if (bias)
+      v += bias_dtype == L3D_F32 ? static_cast<const float*>(bias)[c]
+                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[c]);
+    if (out_dtype == L3D_F32) static_cast<float*>(out)[r * old_ + c] = v;
+    else static_cast<__nv_bfloat16*>(out)[r * old_ + c] = __float2bfloat16_rn(v);
+  }
+}
+
+// Workspace: [0, 256) status word; a bf16 copy of feats (F32 or unaligned
+// rows); an f32 accumulator [n, cout] unless out is an aligned F32 matrix.
+extern "C" size_t l3d_sparse_conv3d_pairs_workspace_size(int64_t n, int64_t cin, int64_t cout) {
+  if (n < 0 || cin < 0 || cout < 0) return 0;
+  return 256 + align256(size_t(n) * size_t(cin) * 2) +
+         align256(size_t(n) * size_t((cout + 3) / 4 * 4) * 4);
+}
+
+extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor* pair_src,
+                                       const l3d_tensor* pair_dest, const l3d_tensor* counts,
+                                       const l3d_tensor* weight, const l3d_tensor* bias,
+                                       const l3d_tensor* out, void* workspace,
+                                       size_t workspace_bytes, l3d_stream stream) {
+  const char* op = "l3d_sparse_conv3d_pairs";
+  using namespace l3d::gemm;
+  if (!feats || !pair_src || !pair_dest || !counts || !weight || !out)
+    return fail(L3D_E_NULL, "%s: feats, pair lists, counts, weight and out are required", op);
+  if (feats->dtype != L3D_BF16 && feats->dtype != L3D_F32)
+    return fail(L3D_E_DTYPE, "%s: feats must be BF16 or F32", op);
+  if (weight->dtype != L3D_BF16) return fail(L3D_E_DTYPE, "%s: weight must be BF16 [27, Cout, Cin]", op);
+  if (pair_src->dtype != L3D_I32 || pair_dest->dtype != L3D_I32 || counts->dtype != L3D_I32)
+    return fail(L3D_E_DTYPE, "%s: pair lists and counts must be I32", op);
+  if (out->dtype != L3D_BF16 && out->dtype != L3D_F32)
+    return fail(L3D_E_DTYPE, "%s: out must be BF16 or F32", op);
+  if (feats->ndim != 2 || weight->ndim != 3 || weight->dims[0] != 27 || out->ndim != 2)
+    return fail(L3D_E_SHAPE, "%s: feats [N, Cin], weight [27, Cout, Cin], out [N, Cout]", op);
+  const int64_t n = feats->dims[0], cin = feats->dims[1], cout = weight->dims[1];
+  if (weight->dims[2] != cin || out->dims[0] != n || out->dims[1] != cout)
+    return fail(L3D_E_SHAPE, "%s: shapes do not agree", op);
+  for (const l3d_tensor* t : {pair_src, pair_dest})
+    if (t->ndim != 2 || t->dims[0] != 27 || t->dims[1] != n)
+      return fail(L3D_E_SHAPE, "%s: pair lists must be [27, N]", op);
+  if (counts->ndim != 1 || counts->dims[0] != 27) return fail(L3D_E_SHAPE, "%s: counts must be [27]", op);
+  if (cin <= 0 || cin % 8 || cout <= 0)
+    return fail(L3D_E_UNSUPPORTED, "%s: Cin must be a positive multiple of 8", op);
+  if (n > INT32_MAX || cout > INT32_MAX) return fail(L3D_E_UNSUPPORTED, "%s: dimensions exceed 2^31", op);
+  if (bias) {
+    if (no_data(bias)) return fail(L3D_E_NULL, "%s: bias has no data", op);
+    if (bias->dtype != L3D_F32 && bias->dtype != L3D_BF16)
+      return fail(L3D_E_DTYPE, "%s: bias must be F32 or BF16", op);
+    if (numel(bias) != cout || (bias->ndim >= 1 && cout > 1 && bias->strides[bias->ndim - 1] != 1))
+      return fail(L3D_E_SHAPE, "%s: bias must be contiguous [Cout]", op);
+  }
+  const size_t need = l3d_sparse_conv3d_pairs_workspace_size(n, cin, cout);
+  if (!workspace || workspace_bytes < need)
+    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(L3D_E_ALIGN, "%s: workspace must be 256-byte aligned", op);
+  if (n == 0) return L3D_OK;
+  if (no_data(feats) || no_data(pair_src) || no_data(pair_dest) || no_data(counts) ||
+      no_data(weight) || no_data(out))
+    return fail(L3D_E_NULL, "%s: null data pointer", op);
+  if ((cin > 1 && feats->strides[1] != 1) || (cout > 1 && out->strides[1] != 1) ||
+      (n > 1 && (pair_src->strides[1] != 1 || pair_dest->strides[1] != 1)) ||
+      counts->strides[0] != 1)
+    return fail(L3D_E_ALIGN, "%s: feats/out rows, pair lists and counts must be contiguous", op);
+  if (weight->strides[2] != 1 || weight->strides[1] != cin || weight->strides[0] != cout * cin)
+    return fail(L3D_E_ALIGN, "%s: weight must be contiguous [27, Cout, Cin]", op);
+  const void* wp = elem_ptr(weight);
+  if (reinterpret_cast<uintptr_t>(wp) % 16) return fail(L3D_E_ALIGN, "%s: weight must be 16-byte aligned", op);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  if (cudaMemsetAsync(status, 0, 256, s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: status clear failed", op);
+  const void* fa = elem_ptr(feats);
+  int64_t fld = n > 1 ? feats->strides[0] : cin;
+  if (feats->dtype == L3D_F32 || (fld * 2) % 16 || reinterpret_cast<uintptr_t>(fa) % 16) {
+    __nv_bfloat16* fb = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+    if (feats->dtype == L3D_F32) {
+      int64_t blocks = (n * cin + 255) / 256;
+      if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
+      f32_to_bf16_kernel<<<int(blocks), 256, 0, s>>>(static_cast<const float*>(fa), fld, n, cin, fb);
+    } else if (cudaMemcpy2DAsync(fb, size_t(cin) * 2, fa, size_t(fld) * 2, size_t(cin) * 2, size_t(n),
+                                 cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+      return fail(L3D_E_CUDA, "%s: feats copy failed", op);
+    }
+    fa = fb;
+    fld = cin;
+  }
+  // f32 accumulator: out itself when it is an aligned F32 matrix.
+  void* outp = const_cast<char*>(elem_ptr(out));
+  const int64_t old_ = n > 1 ? out->strides[0] : cout;
+  float* accp = reinterpret_cast<float*>(ws + 256 + align256(size_t(n) * size_t(cin) * 2));
+  int64_t ald = (cout + 3) / 4 * 4;  // 16-byte aligned rows
+  const bool in_place = out->dtype == L3D_F32 && reinterpret_cast<uintptr_t>(outp) % 16 == 0 &&
+                        (old_ * 4) % 16 == 0;
+  if (in_place) {
+    accp = static_cast<float*>(outp);
+    ald = old_;
+  }
+  if (cudaMemset2DAsync(accp, size_t(ald) * 4, 0, size_t(cout) * 4, size_t(n), s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: accumulator clear failed", op);
+  CUtensorMap map_w;
+  if (!make_map_w27(&map_w, wp, uint64_t(cout), uint64_t(cin)))
+    return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_PAIRS>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ModeCfg<MODE_PAIRS>::SMEM);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
+  Params p{};
+  p.M = int(n);
+  p.N = int(cout);
+  p.cin = int(cin);
+  p.cin_pad = int((cin + BK - 1) / BK * BK);
+  p.K = p.cin_pad;
+  p.y = accp;
+  p.y_ld = ald;
+  p.y_dtype = L3D_F32;
+  p.y_vec = 1;  // accumulator rows are 16-byte aligned (see above)
+  p.status = status;
+  p.feats = static_cast<const __nv_bfloat16*>(fa);
+  p.feats_ld = fld;
+  p.tma_store = 0;
+  const int32_t* src0 = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(pair_src)));
+  const int32_t* dst0 = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(pair_dest)));
+  const int32_t* cnt = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(counts)));
+  const int tiles_max = int(((n + BM - 1) / BM) * ((cout + BN - 1) / BN));
+  const int grid = tiles_max < sm_count() ? tiles_max : sm_count();
+  // One launch per kernel offset, in ascending order (the reference's
+  // index_add order); each reads its pair count on the device.
+  for (int k = 0; k < 27; ++k) {
+    p.koff = k;
+    p.psrc = src0 + int64_t(k) * pair_src->strides[0];
+    p.pdst = dst0 + int64_t(k) * pair_dest->strides[0];
+    p.pcount = cnt + k;
+    qgemm_kernel<MODE_PAIRS><<<grid, THREADS, ModeCfg<MODE_PAIRS>::SMEM, s>>>(map_w, map_w, map_w,
+                                                                              map_w, p);
+  }
+  if (!in_place || bias) {
+    int64_t blocks = (n * cout + 255) / 256;
+    if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
+    conv_finish_kernel<<<int(blocks), 256, 0, s>>>(accp, ald, n, cout, bias ? elem_ptr(bias) : nullptr,
+                                                   bias ? bias->dtype : L3D_F32, outp, old_,
+                                                   out->dtype);
+  }
+  return check_launch(op);
 }

@@ -185,6 +185,20 @@ __global__ void __launch_bounds__(kTile) pair_write_kernel(const int32_t* __rest
   }
 }
 
+// nbr[i, k] = row of coord_i + delta_k, or -1 (the dense form of the pair
+// lists, consumed by the sparse-conv gather GEMM).
+__global__ void neighbor_map_kernel(const int32_t* __restrict__ coords, int64_t cs0, int64_t cs1,
+                                    int64_t n, SparseWs ws, int32_t* __restrict__ nbr,
+                                    int64_t ns0) {
+  const int64_t total = n * 27;
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = t / 27;
+    const int k = int(t - i * 27);
+    nbr[i * ns0 + k] = neighbour(coords, cs0, cs1, i, k, ws);
+  }
+}
+
 template <typename T, typename I>
 __global__ void index_select_kernel(const T* __restrict__ feats, int64_t fs0, int64_t nrows,
                                     const I* __restrict__ ids, int64_t is0, T* __restrict__ out,
@@ -443,5 +457,50 @@ extern "C" int l3d_sparse_neighbor_pairs_noalloc(const l3d_tensor* coords,
                                            static_cast<int32_t*>(pair_dest->data) + pair_dest->offset,
                                            static_cast<int32_t*>(pair_src->data) + pair_src->offset,
                                            n);
+  return check_launch(op);
+}
+
+extern "C" int l3d_sparse_neighbor_map(const l3d_tensor* coords, const l3d_tensor* nbr,
+                                       void* workspace, size_t workspace_bytes,
+                                       l3d_stream stream) {
+  const char* op = "l3d_sparse_neighbor_map";
+  if (!coords || !nbr) return fail(L3D_E_NULL, "%s: coords and nbr are required", op);
+  if (coords->dtype != L3D_I32 || nbr->dtype != L3D_I32)
+    return fail(L3D_E_DTYPE, "%s: coords and nbr must be I32", op);
+  if (coords->ndim != 2 || coords->dims[1] != 3) return fail(L3D_E_SHAPE, "%s: coords [N, 3]", op);
+  const int64_t n = coords->dims[0];
+  if (nbr->ndim != 2 || nbr->dims[0] != n || nbr->dims[1] != 27)
+    return fail(L3D_E_SHAPE, "%s: nbr must be [N, 27]", op);
+  if (n == 0) return L3D_OK;
+  if (no_data(coords) || no_data(nbr)) return fail(L3D_E_NULL, "%s: null data pointer", op);
+  if (n >= (int64_t(1) << 31)) return fail(L3D_E_UNSUPPORTED, "%s: N must fit in I32", op);
+  if (nbr->strides[1] != 1) return fail(L3D_E_ALIGN, "%s: nbr rows must be contiguous", op);
+  const size_t need = sparse_ws_bytes(n);
+  if (!workspace || workspace_bytes < need)
+    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(L3D_E_ALIGN, "%s: workspace must be 256-byte aligned", op);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SparseWs ws;
+  ws.cap = table_cap(n);
+  ws.tiles = (n + kTile - 1) / kTile;
+  char* base = static_cast<char*>(workspace);
+  ws.keys = reinterpret_cast<unsigned long long*>(base);
+  base += align256(ws.cap * 8);
+  ws.vals = reinterpret_cast<int32_t*>(base);
+  ws.tile_counts = nullptr;
+  if (cudaMemsetAsync(ws.keys, 0xff, ws.cap * 8, s) != cudaSuccess ||
+      cudaMemsetAsync(ws.vals, 0xff, ws.cap * 4, s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: workspace clear failed", op);
+  const int32_t* cp = static_cast<const int32_t*>(coords->data) + coords->offset;
+  const int64_t cs0 = coords->strides[0], cs1 = coords->strides[1];
+  int blocks = int((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  hash_insert_kernel<<<blocks, 256, 0, s>>>(cp, cs0, cs1, n, ws);
+  const int64_t total = n * 27;
+  const int64_t cap = int64_t(sm_count()) * 32;
+  blocks = int((total + 255) / 256 < cap ? (total + 255) / 256 : cap);
+  neighbor_map_kernel<<<blocks, 256, 0, s>>>(cp, cs0, cs1, n, ws,
+                                             static_cast<int32_t*>(nbr->data) + nbr->offset,
+                                             nbr->strides[0]);
   return check_launch(op);
 }

@@ -358,3 +358,65 @@ def index_select_rows(feats, ids):
     out = torch.empty((ids.shape[0], feats.shape[1]), dtype=feats.dtype, device=feats.device)
     call("l3d_index_select_rows", ref(desc(feats)), ref(desc(ids)), ref(desc(out)), _s(feats))
     return out
+
+
+def sparse_neighbor_map(coords):
+    """[N, 27] int32 neighbour rows (-1 when absent) of a coordinate set, the
+    dense form of the CoordMap lookups (crate/runtime/trellis2_sparse.rs:68-106)."""
+    _check_cuda(coords)
+    coords = coords.to(torch.int32)
+    n = coords.shape[0]
+    nbr = torch.empty((n, 27), dtype=torch.int32, device=coords.device)
+    need = _lib.lib().l3d_sparse_neighbor_pairs_workspace_size(n)
+    ws = torch.empty(max(need, 256), dtype=torch.uint8, device=coords.device)
+    call("l3d_sparse_neighbor_map", ref(desc(coords)), ref(desc(nbr)), ws.data_ptr(), ws.numel(),
+         _s(coords))
+    return nbr
+
+
+class SparseConv3d:
+    """SparseConv3d (crate/runtime/trellis2_sparse.rs:138-243): submanifold
+    3x3x3 conv.  `weight` is the checkpoint layout [Cout, 3, 3, 3, Cin] or the
+    transposed kernel [27, Cout, Cin]; it is kept on the device as bf16
+    [27, Cout, Cin], the tensor-core operand."""
+
+    def __init__(self, weight, bias=None):
+        _check_cuda(weight, bias)
+        if weight.dim() == 5:
+            cout, cin = weight.shape[0], weight.shape[4]
+            weight = weight.reshape(cout, 27, cin).permute(1, 0, 2)
+        self.weight = weight.to(torch.bfloat16).contiguous()
+        self.cout, self.cin = self.weight.shape[1], self.weight.shape[2]
+        self.bias = bias
+        self._ws = None
+
+    def _workspace(self, need, device):
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        return self._ws
+
+    def __call__(self, feats, pairs=None, coords=None, nbr=None, out_dtype=torch.float32):
+        """Per-offset GEMMs over the neighbour pairs (`pairs` = the
+        (pair_dest, pair_src, counts) of `sparse_neighbor_pairs`, built from
+        `coords` when omitted); with `nbr` (a `sparse_neighbor_map`) instead,
+        one implicit GEMM over all 27 offsets of every row, which pays when
+        most neighbours exist."""
+        _check_cuda(feats, coords, nbr)
+        n = feats.shape[0]
+        out = torch.empty((n, self.cout), dtype=out_dtype, device=feats.device)
+        if nbr is not None:
+            need = _lib.lib().l3d_sparse_conv3d_workspace_size(n, self.cin,
+                                                               _lib._TORCH_TO_L3D[feats.dtype])
+            ws = self._workspace(need, feats.device)
+            call("l3d_sparse_conv3d", ref(desc(feats)), ref(desc(nbr)), ref(desc(self.weight)),
+                 ref(desc(self.bias)), ref(desc(out)), ws.data_ptr(), ws.numel(), _s(feats))
+            return out
+        if pairs is None:
+            pairs = sparse_neighbor_pairs(coords)
+        dest, src, counts = pairs
+        need = _lib.lib().l3d_sparse_conv3d_pairs_workspace_size(n, self.cin, self.cout)
+        ws = self._workspace(need, feats.device)
+        call("l3d_sparse_conv3d_pairs", ref(desc(feats)), ref(desc(src)), ref(desc(dest)),
+             ref(desc(counts)), ref(desc(self.weight)), ref(desc(self.bias)), ref(desc(out)),
+             ws.data_ptr(), ws.numel(), _s(feats))
+        return out

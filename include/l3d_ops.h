@@ -304,6 +304,48 @@ int l3d_dequant_linear_ex(const l3d_tensor* x, const void* wq, int fmt, int64_t 
                           const l3d_tensor* gate, const l3d_tensor* y, void* workspace,
                           size_t workspace_bytes, l3d_stream stream);
 
+/* ---- next row: submanifold sparse conv 3x3x3 ------------------------------------ */
+
+/* Dense neighbour table of a coordinate set: nbr[i, k] = row of coord_i +
+ * delta_k (k = kd*9 + kh*3 + kw, delta = (kd-1, kh-1, kw-1)) or -1; the same
+ * lookups as l3d_sparse_neighbor_pairs (CoordMap, later duplicates win,
+ * crate/runtime/trellis2_sparse.rs:68-106), in [N, 27] I32 form.  Workspace:
+ * l3d_sparse_neighbor_pairs_workspace_size(N) bytes, 256-byte aligned. */
+int l3d_sparse_neighbor_map(const l3d_tensor* coords, const l3d_tensor* nbr, void* workspace,
+                            size_t workspace_bytes, l3d_stream stream);
+
+/* Workspace bytes for l3d_sparse_conv3d on n rows of cin channels. */
+size_t l3d_sparse_conv3d_workspace_size(int64_t n, int64_t cin, int feats_dtype);
+
+/* SparseConv3d::forward (crate/runtime/trellis2_sparse.rs:197-243):
+ * out[i] = bias + sum_k W[k] . feats[nbr[i, k]] (missing neighbours add 0),
+ * as one implicit GEMM on the tensor cores (tcgen05, f32 accumulate): the
+ * neighbour rows are gathered into the operand tile in shared memory, never
+ * materialised.  feats [N, Cin] BF16 (F32 accepted: rounded to BF16), Cin a
+ * multiple of 8; nbr [N, 27] I32 from l3d_sparse_neighbor_map; weight
+ * [27, Cout, Cin] BF16 contiguous (the reference's weight27 layout); bias
+ * [Cout] F32/BF16 or NULL; out [N, Cout] F32/BF16. */
+int l3d_sparse_conv3d(const l3d_tensor* feats, const l3d_tensor* nbr, const l3d_tensor* weight,
+                      const l3d_tensor* bias, const l3d_tensor* out, void* workspace,
+                      size_t workspace_bytes, l3d_stream stream);
+
+/* Workspace bytes for l3d_sparse_conv3d_pairs. */
+size_t l3d_sparse_conv3d_pairs_workspace_size(int64_t n, int64_t cin, int64_t cout);
+
+/* SparseConv3d::forward as the reference computes it
+ * (crate/runtime/trellis2_sparse.rs:211-241): for each kernel offset k in
+ * ascending order, the rows feats[pair_src[k, p]] of its pairs times W[k]^T,
+ * added into out[pair_dest[k, p]] (index_add), then + bias.  One tensor-core
+ * GEMM per offset over its compacted pairs only (work proportional to the
+ * neighbour count, not to 27), accumulated in f32; deterministic.  Pair lists
+ * and counts as written by l3d_sparse_neighbor_pairs; other arguments as for
+ * l3d_sparse_conv3d. */
+int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor* pair_src,
+                            const l3d_tensor* pair_dest, const l3d_tensor* counts,
+                            const l3d_tensor* weight, const l3d_tensor* bias,
+                            const l3d_tensor* out, void* workspace, size_t workspace_bytes,
+                            l3d_stream stream);
+
 /* ---- GGUF tensor index (the on-disk format feeding a13) ------------------------ */
 
 /* One tensor of a GGUF file.  name points into the caller's buffer (not

@@ -36,6 +36,8 @@ def _case(orc, M, N, K, fmt, seed, scale_rows=True):
     (4, 3072, 1024, "q4_0", "f32", True),        # to_kv, tiny M
     (513, 1536, 1536, "q8_0", "bf16", True),     # bf16 output
     (128, 256, 256, "q8_0", "f32", False),       # exactly one tile
+    (64, 100, 256, "q8_0", "bf16", True),        # rows of 200 B: scalar stores (direct path)
+    (700, 100, 512, "q8_0", "f32", True),        # rows of 400 B, decode-once mode
 ])
 def test_dequant_linear_matches_oracle(ops, orc, dev, M, N, K, fmt, ydt, bias):
     import torch
@@ -156,6 +158,7 @@ def _act_ref(name, z):
     (700, 1536, 1024, None, True, True, "bf16"),           # x += gate * linear(h), in place
     (300, 300, 256, "silu", True, False, "f32"),           # N tail, residual without gate
     (37, 520, 1024, None, True, True, "bf16"),             # small M, N tail, gated residual
+    (600, 300, 512, "gelu", True, True, "f32"),            # f32 residual tiles by TMA, N tail
 ])
 def test_dequant_linear_fused_epilogue(ops, orc, dev, M, N, K, act, res, gate, ydt):
     """y = residual + gate * act(x . W^T + b) against the f64 product of the same

@@ -58,10 +58,11 @@ constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 // warps gather the A tile (the 27 neighbour rows of each output row, one
 // kernel offset per Cin-wide stretch of K) and TMA streams the bf16
 // [27, Cout, Cin] weights.
-// MODE_PAIRS is the same conv one kernel offset at a time over its compacted
-// neighbour pairs: rows are gathered through the pair sources and the
-// epilogue adds the product into the pair destinations of an f32
-// accumulator (launched once per offset, in ascending order).
+// MODE_PAIRS is the same conv over the compacted neighbour pairs of all 27
+// offsets in one launch: offset k's pairs form a segment of whole 128-row
+// tiles; a tile gathers its rows through the pair sources, multiplies by
+// W[k] and stores the f32 products (a later pass adds them per output row in
+// offset order).
 enum { MODE_RAW_TMA = 0, MODE_RAW_LDG = 1, MODE_BF16 = 2, MODE_GATHER = 3, MODE_PAIRS = 4 };
 template <int MODE>
 struct ModeCfg {
@@ -296,12 +297,12 @@ struct Params {
   const __nv_bfloat16* feats;      // rows of feats_ld elements
   int64_t feats_ld;
   int cin, cin_pad;                // cin_pad = cin rounded up to BK
-  // MODE_PAIRS: rows m < *pcount: A[m] = feats[psrc[m]], y[pdst[m]] += acc[m]
-  // (f32 y); the weights of offset koff.
+  // MODE_PAIRS: segment k = tiles [seg_tile[k], seg_tile[k + 1]) holds the
+  // seg_count[k] pairs of offset k, A rows feats[psrc[k * pstride + j]].
   const int32_t* psrc;
-  const int32_t* pdst;
-  const int32_t* pcount;
-  int koff;
+  int64_t pstride;
+  int seg_tile[28];
+  int seg_count[27];
 };
 
 // The fused epilogue ops on NC consecutive columns [col0, col0 + NC) of one
@@ -453,9 +454,12 @@ __device__ __forceinline__ void dequant_tile(const Params& p, const uint8_t* raw
 // 4 chunks each: thread t takes chunk t % 8 of rows t / 8 + 32 i; src[] holds
 // the rows' neighbours for the current kernel offset and is reloaded only
 // when the offset changes.
+// PAIRS: m0 is the tile's first row within its segment, `rows` the
+// segment's pair count and `psrc` its pair sources.
 template <bool PAIRS>
 __device__ __forceinline__ void gather_tile(const Params& p, uint8_t* tile, int m0, int kb, int t,
-                                            int rows, int& cur_off, int32_t (&src)[4]) {
+                                            int rows, const int32_t* psrc, int& cur_off,
+                                            int32_t (&src)[4]) {
   const int kk = kb * BK;
   const int off = PAIRS ? 0 : kk / p.cin_pad, c0 = kk - off * p.cin_pad;
   if (off != cur_off) {
@@ -463,23 +467,23 @@ __device__ __forceinline__ void gather_tile(const Params& p, uint8_t* tile, int 
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int row = m0 + (t >> 3) + 32 * i;
-      if constexpr (PAIRS) src[i] = row < rows ? __ldg(p.psrc + row) : -1;
+      if constexpr (PAIRS) src[i] = row < rows ? __ldg(psrc + row) : -1;
       else src[i] = row < rows ? __ldg(p.nbr + int64_t(row) * 27 + off) : -1;
     }
   }
   const int j = t & 7;
   const int c = c0 + 8 * j;
-  uint4 v[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (src[i] >= 0 && c < p.cin)
-      v[i] = __ldg(reinterpret_cast<const uint4*>(p.feats + int64_t(src[i]) * p.feats_ld + c));
-  }
+  // 16-byte asynchronous copies straight into the swizzled tile; a missing
+  // neighbour (or a channel past cin) copies 0 source bytes and zero-fills.
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = (t >> 3) + 32 * i;
-    *reinterpret_cast<uint4*>(tile + r * 128 + ((j ^ (r & 7)) << 4)) = v[i];
+    const bool ok = src[i] >= 0 && c < p.cin;
+    const __nv_bfloat16* g = ok ? p.feats + int64_t(src[i]) * p.feats_ld + c : p.feats;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     smem_u32(tile + r * 128 + ((j ^ (r & 7)) << 4))),
+                 "l"(g), "r"(ok ? 16u : 0u)
+                 : "memory");
   }
 }
 
@@ -513,9 +517,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* rbars = bars + 3 * STAGES + 7;         // [4][2] residual TMA -> epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Rows of the output (MODE_PAIRS: this offset's pair count, on the device).
-  int rows_m = p.M;
-  if constexpr (PAIRS) rows_m = min(__ldg(p.pcount), p.M);
+  // MODE_PAIRS: segment boundaries (in tiles) and pair counts per offset.
+  __shared__ int s_seg[28], s_cnt[27];
+  if constexpr (PAIRS) {
+    if (threadIdx.x < 28) s_seg[threadIdx.x] = p.seg_tile[threadIdx.x];
+    if (threadIdx.x < 27) s_cnt[threadIdx.x] = p.seg_count[threadIdx.x];
+  }
+  auto seg_of = [&](int mt) {  // offset whose segment holds row tile mt
+    int k = 0;
+    while (k < 26 && mt >= s_seg[k + 1]) ++k;
+    return k;
+  };
+  const int rows_m = p.M;
   const int num_m = (rows_m + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
   const int tiles = num_m * num_n;
   const int kblocks = (p.K + BK - 1) / BK;
@@ -562,7 +575,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // Weights [27, Cout, Cin]: box of 64 channels x 256 outputs of one offset.
             const int kk = kb * BK, off = PAIRS ? 0 : kk / p.cin_pad;
             tma_load_3d(sb + stage * B_BYTES, &map_w, &lfull[stage], kk - off * p.cin_pad, n0,
-                        PAIRS ? p.koff : off);
+                        PAIRS ? seg_of(m0 / BM) : off);
           } else {
             tma_load_2d(sa + stage * A_BYTES, &map_x, &lfull[stage], kb * BK, m0);
           }
@@ -758,6 +771,36 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (lane == 0 && ci + 1 < BN / EPI_COLS) issue_res(m0, n0, ci + 1);
             }
           }
+          if (f32 && !tres) {
+            // f32 without a residual: each 32-column half is its own store
+            // from its own 4 KB staging half, so one half is written while
+            // the other's store is still reading.
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (col0 + 32 * h >= p.N) break;  // warp-uniform
+              uint8_t* hbuf = stg + h * 4096;
+              if (lane == 0) {
+                if (last_b != h) bulk_wait_read1();
+                else bulk_wait_read0();
+              }
+              __syncwarp();
+              uint8_t* rowp = hbuf + lane * 128;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int q = 8 * h + j;
+                *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              }
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&map_y, hbuf, col0 + 32 * h, m0 + quarter * 32);
+                bulk_commit();
+              }
+              last_b = h;
+            }
+            continue;
+          }
           if (lane == 0) {
             // The store that last read this staging has finished reading it
             // (bf16 without residual: the newest store may still be reading
@@ -808,21 +851,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(taddr + uint32_t(c), v);
         const int col0 = n0 + c;
         if (row < rows_m && col0 < p.N) {
-          if constexpr (PAIRS) {
-            // y[pdst[row]] += acc (f32 accumulator; rows are distinct per offset).
-            float* yr = static_cast<float*>(p.y) + int64_t(__ldg(p.pdst + row)) * p.y_ld + col0;
-            if (col0 + 32 <= p.N && p.y_vec) {
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                float4 a = *reinterpret_cast<const float4*>(yr + q * 4);
-                a.x += v[q * 4]; a.y += v[q * 4 + 1]; a.z += v[q * 4 + 2]; a.w += v[q * 4 + 3];
-                *reinterpret_cast<float4*>(yr + q * 4) = a;
-              }
-            } else {
-              for (int i = 0; i < 32 && col0 + i < p.N; ++i) yr[i] += v[i];
-            }
-            continue;
-          }
           if (p.bias) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -870,6 +898,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int t = threadIdx.x - 6 * 32;  // 0 .. 255
     int stage = 0;
     uint32_t phase = 0;
+    // Gather modes keep up to kGatherDepth stages of cp.async copies in
+    // flight; a stage is signalled to the MMA once its copies have landed
+    // (cp.async.wait_group) and a proxy fence has made them visible to the
+    // tensor core.  kGatherDepth < STAGES, so the producer can always refill
+    // the stages the gatherers wait on.
+    constexpr int kGatherDepth = 3;
+    int pend = 0, arr_stage = 0;
+    auto retire_oldest = [&](bool all) {
+      if (all) asm volatile("cp.async.wait_group 0;" ::: "memory");
+      else asm volatile("cp.async.wait_group %0;" ::"n"(kGatherDepth - 1) : "memory");
+      do {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[arr_stage]);
+        if (++arr_stage == STAGES) arr_stage = 0;
+        --pend;
+      } while (all && pend > 0);
+    };
     for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
       const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
       int cur_off = -1;
@@ -883,18 +929,31 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         if constexpr (GATHER) {
-          gather_tile<PAIRS>(p, sa + stage * A_BYTES, m0, kb, t, rows_m, cur_off, src);
+          if constexpr (PAIRS) {
+            const int k = seg_of(m0 / BM);
+            gather_tile<true>(p, sa + stage * A_BYTES, m0 - s_seg[k] * BM, kb, t, s_cnt[k],
+                              p.psrc + int64_t(k) * p.pstride, cur_off, src);
+          } else {
+            gather_tile<false>(p, sa + stage * A_BYTES, m0, kb, t, rows_m, nullptr, cur_off, src);
+          }
+          asm volatile("cp.async.commit_group;" ::: "memory");
+          if (++pend == kGatherDepth) retire_oldest(false);
         } else {
           (void)m0;
           dequant_tile<RAW_TMA>(p, sr + stage * RAWB, sb + stage * B_BYTES, n0, kb, t);
+          // Generic-proxy smem writes must be visible to the tensor core.
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bfull[stage]);
         }
-        // Generic-proxy smem writes must be visible to the tensor core.
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bfull[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
+    }
+    // Copies still in flight land before teardown (and their stages are
+    // signalled, for an MMA that may still be waiting on them).
+    if constexpr (GATHER) {
+      if (pend > 0) retire_oldest(true);
     }
   }
 
@@ -1355,40 +1414,141 @@ extern "C" int l3d_sparse_conv3d(const l3d_tensor* feats, const l3d_tensor* nbr,
 }
 
 // ------------------------------------------------- sparse conv over pair lists
-// acc [n, cout] f32 rows of ld elements -> out = acc + bias (out's dtype).
-__global__ void conv_finish_kernel(const float* __restrict__ acc, int64_t ald, int64_t n,
-                                   int64_t cout, const void* bias, int bias_dtype, void* out,
-                                   int64_t old_, int out_dtype) {
-  const int64_t total = n * cout;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t r = i / cout, c = i - r * cout;
-    float v = acc[r * ald + c];
-    if (bias)
-      v += bias_dtype == L3D_F32 ? static_cast<const float*>(bias)[c]
-                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[c]);
-    if (out_dtype == L3D_F32) static_cast<float*>(out)[r * old_ + c] = v;
-    else static_cast<__nv_bfloat16*>(out)[r * old_ + c] = __float2bfloat16_rn(v);
+// pos[dest_k[j] * 27 + k] = j: where row i's product for offset k sits in
+// offset k's pair list (-1 when i has no neighbour at k; cleared before).
+__global__ void pair_pos_kernel(const int32_t* __restrict__ dest, int64_t dstride,
+                                const int32_t* __restrict__ counts, int64_t n,
+                                int32_t* __restrict__ pos) {
+  const int k = blockIdx.y;
+  const int64_t cnt = __ldg(counts + k) < n ? __ldg(counts + k) : n;
+  for (int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < cnt;
+       j += int64_t(gridDim.x) * blockDim.x)
+    pos[int64_t(__ldg(dest + k * dstride + j)) * 27 + k] = int32_t(j);
+}
+
+// out[i, c] = ((0 + prod_0) + prod_1) + ... + prod_26 + bias[c]: each row's
+// products added in ascending offset order (the reference's index_add
+// order), then the bias; f32, rounded once to out's dtype.  One warp per row:
+// lane k < 27 reads the row's position in offset k's segment once, and the
+// lanes sum 4 columns each per 128-column step.
+__global__ void pair_reduce_kernel(const float* __restrict__ prod, int64_t pld,
+                                   const int32_t* __restrict__ pos, const int64_t* __restrict__ seg_row,
+                                   int64_t n, int64_t cout, const void* bias, int bias_dtype,
+                                   void* out, int64_t old_, int out_dtype) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int64_t srow = lane < 27 ? __ldg(seg_row + lane) : 0;
+  for (int64_t i = warp0; i < n; i += nwarps) {
+    const int32_t j = lane < 27 ? __ldg(pos + i * 27 + lane) : -1;
+    const int64_t prow = j >= 0 ? srow + j : -1;  // product row of offset `lane`
+    const unsigned have = __ballot_sync(0xffffffffu, j >= 0);
+    // Warp-uniform column loop (every lane takes part in the shuffles).
+    for (int64_t cb = 0; cb < cout; cb += 128) {
+      const int64_t c = cb + 4 * lane;
+      const bool active = c < cout;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool full = c + 4 <= cout;
+      unsigned m = have;
+      while (m) {  // offsets with a neighbour, ascending, up to 4 loads in flight
+        int64_t r[4];
+        int cnt = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          r[q] = -1;
+          if (m) {
+            const int k = __ffs(m) - 1;
+            m &= m - 1;
+            r[q] = __shfl_sync(0xffffffffu, prow, k);
+            ++cnt;
+          }
+        }
+        if (!active) continue;
+        float4 v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (q < cnt) {
+            const float* src = prod + r[q] * pld + c;
+            if (full) {
+              v[q] = __ldg(reinterpret_cast<const float4*>(src));
+            } else {
+              v[q].x = __ldg(src);
+              if (c + 1 < cout) v[q].y = __ldg(src + 1);
+              if (c + 2 < cout) v[q].z = __ldg(src + 2);
+            }
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (q < cnt) {
+            acc.x += v[q].x; acc.y += v[q].y; acc.z += v[q].z; acc.w += v[q].w;
+          }
+        }
+      }
+      if (!active) continue;
+      const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t col = c + e;
+        if (col >= cout) break;
+        float v = vals[e];
+        if (bias)
+          v += bias_dtype == L3D_F32 ? static_cast<const float*>(bias)[col]
+                                     : __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[col]);
+        if (out_dtype == L3D_F32) static_cast<float*>(out)[i * old_ + col] = v;
+        else static_cast<__nv_bfloat16*>(out)[i * old_ + col] = __float2bfloat16_rn(v);
+      }
+    }
   }
 }
 
-// Workspace: [0, 256) status word; a bf16 copy of feats (F32 or unaligned
-// rows); an f32 accumulator [n, cout] unless out is an aligned F32 matrix.
-extern "C" size_t l3d_sparse_conv3d_pairs_workspace_size(int64_t n, int64_t cin, int64_t cout) {
-  if (n < 0 || cin < 0 || cout < 0) return 0;
-  return 256 + align256(size_t(n) * size_t(cin) * 2) +
-         align256(size_t(n) * size_t((cout + 3) / 4 * 4) * 4);
+namespace {
+struct PairsLayout {
+  int seg_tile[28];     // prefix of ceil(count_k / 128), in 128-row tiles
+  int64_t rows;         // padded product rows
+  int64_t ld;           // product row stride (floats, multiple of 4)
+  size_t feats_off, prod_off, pos_off, seg_off, total;
+};
+PairsLayout pairs_layout(int64_t n, int64_t cin, int64_t cout, const int32_t* counts_host) {
+  PairsLayout L{};
+  int64_t t = 0;
+  for (int k = 0; k < 27; ++k) {
+    L.seg_tile[k] = int(t);
+    const int64_t c = counts_host[k] < 0 ? 0 : (counts_host[k] > n ? n : counts_host[k]);
+    t += (c + l3d::gemm::BM - 1) / l3d::gemm::BM;
+  }
+  L.seg_tile[27] = int(t);
+  L.rows = t * l3d::gemm::BM;
+  L.ld = (cout + 3) / 4 * 4;
+  L.feats_off = 256;
+  L.prod_off = L.feats_off + align256(size_t(n) * size_t(cin) * 2);
+  L.pos_off = L.prod_off + align256(size_t(L.rows) * size_t(L.ld) * 4);
+  L.seg_off = L.pos_off + align256(size_t(n) * 27 * 4);
+  L.total = L.seg_off + 256;
+  return L;
+}
+}  // namespace
+
+// Workspace: status word, a bf16 copy of feats (F32 or unaligned rows), the
+// f32 products of every pair (segments padded to 128 rows), the [N, 27]
+// position table and the segment row offsets.
+extern "C" size_t l3d_sparse_conv3d_pairs_workspace_size(int64_t n, int64_t cin, int64_t cout,
+                                                         const int32_t* counts_host) {
+  if (n < 0 || cin < 0 || cout < 0 || !counts_host) return 0;
+  return pairs_layout(n, cin, cout, counts_host).total;
 }
 
 extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor* pair_src,
                                        const l3d_tensor* pair_dest, const l3d_tensor* counts,
-                                       const l3d_tensor* weight, const l3d_tensor* bias,
-                                       const l3d_tensor* out, void* workspace,
-                                       size_t workspace_bytes, l3d_stream stream) {
+                                       const int32_t* counts_host, const l3d_tensor* weight,
+                                       const l3d_tensor* bias, const l3d_tensor* out,
+                                       void* workspace, size_t workspace_bytes,
+                                       l3d_stream stream) {
   const char* op = "l3d_sparse_conv3d_pairs";
   using namespace l3d::gemm;
-  if (!feats || !pair_src || !pair_dest || !counts || !weight || !out)
-    return fail(L3D_E_NULL, "%s: feats, pair lists, counts, weight and out are required", op);
+  if (!feats || !pair_src || !pair_dest || !counts || !counts_host || !weight || !out)
+    return fail(L3D_E_NULL, "%s: feats, pair lists, counts (device and host), weight and out are required", op);
   if (feats->dtype != L3D_BF16 && feats->dtype != L3D_F32)
     return fail(L3D_E_DTYPE, "%s: feats must be BF16 or F32", op);
   if (weight->dtype != L3D_BF16) return fail(L3D_E_DTYPE, "%s: weight must be BF16 [27, Cout, Cin]", op);
@@ -1405,6 +1565,9 @@ extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor
     if (t->ndim != 2 || t->dims[0] != 27 || t->dims[1] != n)
       return fail(L3D_E_SHAPE, "%s: pair lists must be [27, N]", op);
   if (counts->ndim != 1 || counts->dims[0] != 27) return fail(L3D_E_SHAPE, "%s: counts must be [27]", op);
+  for (int k = 0; k < 27; ++k)
+    if (counts_host[k] < 0 || counts_host[k] > n)
+      return fail(L3D_E_SHAPE, "%s: counts_host[%d] out of range", op, k);
   if (cin <= 0 || cin % 8 || cout <= 0)
     return fail(L3D_E_UNSUPPORTED, "%s: Cin must be a positive multiple of 8", op);
   if (n > INT32_MAX || cout > INT32_MAX) return fail(L3D_E_UNSUPPORTED, "%s: dimensions exceed 2^31", op);
@@ -1415,9 +1578,10 @@ extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor
     if (numel(bias) != cout || (bias->ndim >= 1 && cout > 1 && bias->strides[bias->ndim - 1] != 1))
       return fail(L3D_E_SHAPE, "%s: bias must be contiguous [Cout]", op);
   }
-  const size_t need = l3d_sparse_conv3d_pairs_workspace_size(n, cin, cout);
-  if (!workspace || workspace_bytes < need)
-    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
+  const PairsLayout L = pairs_layout(n, cin, cout, counts_host);
+  if (L.rows > INT32_MAX) return fail(L3D_E_UNSUPPORTED, "%s: too many pairs", op);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, L.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(L3D_E_ALIGN, "%s: workspace must be 256-byte aligned", op);
   if (n == 0) return L3D_OK;
@@ -1440,7 +1604,7 @@ extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor
   const void* fa = elem_ptr(feats);
   int64_t fld = n > 1 ? feats->strides[0] : cin;
   if (feats->dtype == L3D_F32 || (fld * 2) % 16 || reinterpret_cast<uintptr_t>(fa) % 16) {
-    __nv_bfloat16* fb = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+    __nv_bfloat16* fb = reinterpret_cast<__nv_bfloat16*>(ws + L.feats_off);
     if (feats->dtype == L3D_F32) {
       int64_t blocks = (n * cin + 255) / 256;
       if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
@@ -1452,66 +1616,69 @@ extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor
     fa = fb;
     fld = cin;
   }
-  // f32 accumulator: out itself when it is an aligned F32 matrix.
-  void* outp = const_cast<char*>(elem_ptr(out));
-  const int64_t old_ = n > 1 ? out->strides[0] : cout;
-  float* accp = reinterpret_cast<float*>(ws + 256 + align256(size_t(n) * size_t(cin) * 2));
-  int64_t ald = (cout + 3) / 4 * 4;  // 16-byte aligned rows
-  const bool in_place = out->dtype == L3D_F32 && reinterpret_cast<uintptr_t>(outp) % 16 == 0 &&
-                        (old_ * 4) % 16 == 0;
-  if (in_place) {
-    accp = static_cast<float*>(outp);
-    ald = old_;
-  }
-  if (cudaMemset2DAsync(accp, size_t(ald) * 4, 0, size_t(cout) * 4, size_t(n), s) != cudaSuccess)
-    return fail(L3D_E_CUDA, "%s: accumulator clear failed", op);
-  CUtensorMap map_w;
-  if (!make_map_w27(&map_w, wp, uint64_t(cout), uint64_t(cin)))
-    return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_PAIRS>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ModeCfg<MODE_PAIRS>::SMEM);
-  });
-  if (attr_err != cudaSuccess)
-    return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
-  Params p{};
-  p.M = int(n);
-  p.N = int(cout);
-  p.cin = int(cin);
-  p.cin_pad = int((cin + BK - 1) / BK * BK);
-  p.K = p.cin_pad;
-  p.y = accp;
-  p.y_ld = ald;
-  p.y_dtype = L3D_F32;
-  p.y_vec = 1;  // accumulator rows are 16-byte aligned (see above)
-  p.status = status;
-  p.feats = static_cast<const __nv_bfloat16*>(fa);
-  p.feats_ld = fld;
-  p.tma_store = 0;
+  float* prod = reinterpret_cast<float*>(ws + L.prod_off);
+  int32_t* pos = reinterpret_cast<int32_t*>(ws + L.pos_off);
+  int64_t* segrow = reinterpret_cast<int64_t*>(ws + L.seg_off);
   const int32_t* src0 = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(pair_src)));
   const int32_t* dst0 = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(pair_dest)));
   const int32_t* cnt = static_cast<const int32_t*>(static_cast<const void*>(elem_ptr(counts)));
-  const int tiles_max = int(((n + BM - 1) / BM) * ((cout + BN - 1) / BN));
-  const int grid = tiles_max < sm_count() ? tiles_max : sm_count();
-  // One launch per kernel offset, in ascending order (the reference's
-  // index_add order); each reads its pair count on the device.
-  for (int k = 0; k < 27; ++k) {
-    p.koff = k;
-    p.psrc = src0 + int64_t(k) * pair_src->strides[0];
-    p.pdst = dst0 + int64_t(k) * pair_dest->strides[0];
-    p.pcount = cnt + k;
-    qgemm_kernel<MODE_PAIRS><<<grid, THREADS, ModeCfg<MODE_PAIRS>::SMEM, s>>>(map_w, map_w, map_w,
+  // Position table and segment row offsets.
+  int64_t seg_rows_host[27];
+  for (int k = 0; k < 27; ++k) seg_rows_host[k] = int64_t(L.seg_tile[k]) * BM;
+  if (cudaMemsetAsync(pos, 0xff, size_t(n) * 27 * 4, s) != cudaSuccess ||
+      cudaMemcpyAsync(segrow, seg_rows_host, sizeof(seg_rows_host), cudaMemcpyHostToDevice, s) !=
+          cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: workspace set-up failed", op);
+  {
+    const int64_t bx = (n + 255) / 256 < 64 ? (n + 255) / 256 : 64;
+    pair_pos_kernel<<<dim3(unsigned(bx), 27), 256, 0, s>>>(dst0, pair_dest->strides[0], cnt, n, pos);
+  }
+  // One tensor-core launch over every offset's pair segment.
+  if (L.rows > 0) {
+    Params p{};
+    p.M = int(L.rows);
+    p.N = int(cout);
+    p.cin = int(cin);
+    p.cin_pad = int((cin + BK - 1) / BK * BK);
+    p.K = p.cin_pad;
+    p.y = prod;
+    p.y_ld = L.ld;
+    p.y_dtype = L3D_F32;
+    p.y_vec = 1;
+    p.status = status;
+    p.feats = static_cast<const __nv_bfloat16*>(fa);
+    p.feats_ld = fld;
+    p.psrc = src0;
+    p.pstride = pair_src->strides[0];
+    for (int k = 0; k < 28; ++k) p.seg_tile[k] = L.seg_tile[k];
+    for (int k = 0; k < 27; ++k) p.seg_count[k] = counts_host[k];
+    CUtensorMap map_w, map_y;
+    if (!make_map_w27(&map_w, wp, uint64_t(cout), uint64_t(cin)))
+      return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
+    p.tma_store = make_map_y(&map_y, prod, L3D_F32, uint64_t(L.rows), uint64_t(cout), uint64_t(L.ld)) ? 1 : 0;
+    if (!p.tma_store) map_y = map_w;  // unused
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_PAIRS>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      ModeCfg<MODE_PAIRS>::SMEM);
+    });
+    if (attr_err != cudaSuccess)
+      return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
+    const int tiles = int((L.rows / BM) * ((cout + BN - 1) / BN));
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    qgemm_kernel<MODE_PAIRS><<<grid, THREADS, ModeCfg<MODE_PAIRS>::SMEM, s>>>(map_w, map_w, map_y,
                                                                               map_w, p);
   }
-  if (!in_place || bias) {
-    int64_t blocks = (n * cout + 255) / 256;
+  {
+    int64_t blocks = (n + 7) / 8;  // a warp per row, 8 warps per block
     if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
-    conv_finish_kernel<<<int(blocks), 256, 0, s>>>(accp, ald, n, cout, bias ? elem_ptr(bias) : nullptr,
-                                                   bias ? bias->dtype : L3D_F32, outp, old_,
-                                                   out->dtype);
+    pair_reduce_kernel<<<int(blocks), 256, 0, s>>>(prod, L.ld, pos, segrow, n, cout,
+                                                   bias ? elem_ptr(bias) : nullptr,
+                                                   bias ? bias->dtype : L3D_F32,
+                                                   const_cast<char*>(elem_ptr(out)),
+                                                   n > 1 ? out->strides[0] : cout, out->dtype);
   }
   return check_launch(op);
 }

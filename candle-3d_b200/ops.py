@@ -9,6 +9,7 @@ Invalid inputs raise `L3dError` carrying the library's status and message.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -413,10 +414,15 @@ class SparseConv3d:
             return out
         if pairs is None:
             pairs = sparse_neighbor_pairs(coords)
-        dest, src, counts = pairs
-        need = _lib.lib().l3d_sparse_conv3d_pairs_workspace_size(n, self.cin, self.cout)
+        dest, src, counts = pairs[:3]
+        # The 27 counts on the host size the launch; pass them as a fourth
+        # element of `pairs` to avoid reading them back on every call.
+        counts_host = pairs[3] if len(pairs) > 3 else counts.cpu().numpy()
+        counts_host = np.ascontiguousarray(counts_host, dtype=np.int32)
+        chp = counts_host.ctypes.data
+        need = _lib.lib().l3d_sparse_conv3d_pairs_workspace_size(n, self.cin, self.cout, chp)
         ws = self._workspace(need, feats.device)
         call("l3d_sparse_conv3d_pairs", ref(desc(feats)), ref(desc(src)), ref(desc(dest)),
-             ref(desc(counts)), ref(desc(self.weight)), ref(desc(self.bias)), ref(desc(out)),
-             ws.data_ptr(), ws.numel(), _s(feats))
+             ref(desc(counts)), chp, ref(desc(self.weight)), ref(desc(self.bias)),
+             ref(desc(out)), ws.data_ptr(), ws.numel(), _s(feats))
         return out

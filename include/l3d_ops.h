@@ -329,22 +329,28 @@ int l3d_sparse_conv3d(const l3d_tensor* feats, const l3d_tensor* nbr, const l3d_
                       const l3d_tensor* bias, const l3d_tensor* out, void* workspace,
                       size_t workspace_bytes, l3d_stream stream);
 
-/* Workspace bytes for l3d_sparse_conv3d_pairs. */
-size_t l3d_sparse_conv3d_pairs_workspace_size(int64_t n, int64_t cin, int64_t cout);
+/* Workspace bytes for l3d_sparse_conv3d_pairs (counts_host: the 27 pair
+ * counts, as in `counts`, read on the host). */
+size_t l3d_sparse_conv3d_pairs_workspace_size(int64_t n, int64_t cin, int64_t cout,
+                                              const int32_t* counts_host);
 
 /* SparseConv3d::forward as the reference computes it
- * (crate/runtime/trellis2_sparse.rs:211-241): for each kernel offset k in
- * ascending order, the rows feats[pair_src[k, p]] of its pairs times W[k]^T,
- * added into out[pair_dest[k, p]] (index_add), then + bias.  One tensor-core
- * GEMM per offset over its compacted pairs only (work proportional to the
- * neighbour count, not to 27), accumulated in f32; deterministic.  Pair lists
- * and counts as written by l3d_sparse_neighbor_pairs; other arguments as for
+ * (crate/runtime/trellis2_sparse.rs:211-241): for each kernel offset k, the
+ * rows feats[pair_src[k, p]] of its pairs times W[k]^T, added into
+ * out[pair_dest[k, p]] in ascending k (index_add), then + bias.  One
+ * tensor-core launch multiplies the pairs of all offsets (each offset's pairs
+ * a segment of 128-row tiles, so the work follows the neighbour count, not
+ * 27 x N), storing f32 products; a second pass adds each output row's
+ * products in ascending offset order, then the bias - the reference's
+ * summation order, deterministic.  Pair lists and device counts as written by
+ * l3d_sparse_neighbor_pairs; counts_host holds the same 27 counts in host
+ * memory (they size the launch and the workspace); other arguments as for
  * l3d_sparse_conv3d. */
 int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor* pair_src,
                             const l3d_tensor* pair_dest, const l3d_tensor* counts,
-                            const l3d_tensor* weight, const l3d_tensor* bias,
-                            const l3d_tensor* out, void* workspace, size_t workspace_bytes,
-                            l3d_stream stream);
+                            const int32_t* counts_host, const l3d_tensor* weight,
+                            const l3d_tensor* bias, const l3d_tensor* out, void* workspace,
+                            size_t workspace_bytes, l3d_stream stream);
 
 /* ---- GGUF tensor index (the on-disk format feeding a13) ------------------------ */
 

@@ -1,0 +1,472 @@
+// Scaled dot-product attention (the attention core of the block stacks,
+// exact_sdpa_heads / exact_query_chunked_sdpa, crate/runtime/
+// attention_math.rs:199-259) on the 5th-generation tensor cores.
+//
+//   out[b, h, i, :] = softmax_j(q[b,h,i,:] . k[b,h,j,:] * scale) v[b,h,j,:]
+//
+// One CTA per (128-query tile, head, batch), 6 warps:
+//   warp 0     TMA producer: the Q tile once, then a 2-stage ring of K tiles
+//              (128 keys x D) and V^T tiles (D x 128 keys; V is transposed
+//              once per call into the workspace so that both products take
+//              K-major operands);
+//   warp 1     MMA issuer: S = Q K^T (M 128, N 128, K D) into TMEM, then
+//              O += P V^T (M 128, N D, K 128) once P is ready;
+//   warps 2-5  softmax / epilogue, one query row per thread (its TMEM lane):
+//              pass 1 reads S and forms the row max, the running O is rescaled
+//              in TMEM when the max grows, pass 2 writes P = exp2(S * scale
+//              * log2 e - m) as bf16 into the 128B-swizzled operand tile and
+//              accumulates the row sum; after the last tile O / l is stored.
+// TMEM: S in columns [0, 128), O in [128, 128 + D) - 256 columns, so two CTAs
+// share an SM.  Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry
+// the CTA records an error in the workspace status word and stops.
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace l3d {
+namespace attn {
+
+using namespace l3d::tc;
+
+constexpr int BQ = 128, BKV = 128;
+constexpr int THREADS = 6 * 32;
+constexpr int TMEM_COLS = 256;
+constexpr int ST_TIMEOUT = 5;
+
+template <int D>
+struct Cfg {
+  static constexpr int DC = D / 64;                   // 64-wide K atoms of Q / K
+  static constexpr int Q_BYTES = BQ * D * 2;
+  static constexpr int K_BYTES = BKV * D * 2;
+  static constexpr int V_BYTES = D * BKV * 2;         // V^T tile: D rows x 128 keys
+  static constexpr int P_BYTES = BQ * BKV * 2;
+  static constexpr int STAGES = 2;
+  static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 1024 + 256;
+  static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
+  static constexpr uint32_t IDESC_O = make_idesc(128, D);
+};
+
+struct Params {
+  int64_t nq, nk;       // query / key lengths
+  int q_hn, k_hn;       // the q / k maps list heads before rows (token-major memory)
+  float scale_log2;     // softmax scale * log2(e)
+  void* out;            // [B, H, nq, D] bf16
+  int64_t ob, oh, on;   // out strides (elements)
+  int* status;
+};
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
+
+// 32 consecutive f32 TMEM columns of this thread's lane <- registers.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, 2)
+    attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                const __grid_constant__ CUtensorMap map_vt, const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sq = smem;                                  // [DC][128 x 64]
+  uint8_t* sk = sq + C::Q_BYTES;                       // [STAGES][DC][128 x 64]
+  uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][2][D x 64]
+  uint8_t* sp = sv + C::STAGES * C::V_BYTES;           // [2][128 x 64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + C::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;        // [STAGES]
+  uint64_t* kv_empty = bars + 3;       // [STAGES]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pv_done = bars + 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 9);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  const int nkv = int((p.nk + BKV - 1) / BKV);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t t_s = tmem_base, t_o = tmem_base + BKV;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_expect_tx(q_full, C::Q_BYTES);
+      for (int dc = 0; dc < C::DC; ++dc)
+        tma_load_4d(sq + dc * (BQ * 128), &map_q, q_full, dc * 64, p.q_hn ? h : q0,
+                    p.q_hn ? q0 : h, b);
+      for (int j = 0; j < nkv && !*abort_flag; ++j) {
+        const int s = j & 1;
+        if (j >= C::STAGES &&
+            !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status, ST_TIMEOUT))
+          break;
+        mbar_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
+        uint8_t* kt = sk + s * C::K_BYTES;
+        for (int dc = 0; dc < C::DC; ++dc)
+          tma_load_4d(kt + dc * (BKV * 128), &map_k, &kv_full[s], dc * 64, p.k_hn ? h : j * BKV,
+                      p.k_hn ? j * BKV : h, b);
+        uint8_t* vt = sv + s * C::V_BYTES;
+        for (int kc = 0; kc < 2; ++kc)
+          tma_load_4d(vt + kc * (D * 128), &map_vt, &kv_full[s], j * BKV + kc * 64, 0, h, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, ST_TIMEOUT)) break;
+        // S is free once the softmax warps have read the previous tile's S.
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) break;
+        tc_fence_after();
+        const uint8_t* kt = sk + s * C::K_BYTES;
+#pragma unroll
+        for (int dc = 0; dc < C::DC; ++dc) {
+          const uint64_t da = smem_desc_sw128(sq + dc * (BQ * 128));
+          const uint64_t db = smem_desc_sw128(kt + dc * (BKV * 128));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16<C::IDESC_S>(t_s, da + uint64_t(2 * k), db + uint64_t(2 * k), (dc | k) ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        // O += P V^T once the softmax warps have written P (and rescaled O).
+        if (!mbar_wait(p_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) break;
+        tc_fence_after();
+        const uint8_t* vt = sv + s * C::V_BYTES;
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc) {
+          const uint64_t da = smem_desc_sw128(sp + kc * (BQ * 128));
+          const uint64_t db = smem_desc_sw128(vt + kc * (D * 128));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16<C::IDESC_O>(t_o, da + uint64_t(2 * k), db + uint64_t(2 * k),
+                                 (j | kc | k) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[s]);
+        umma_commit(pv_done);
+      }
+    }
+  } else {
+    // ------------------------------------------------------ softmax / epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;           // query row within the tile
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait_idle(s_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+      tc_fence_after();
+      const int kvalid = int(p.nk - int64_t(j) * BKV);  // keys of this tile (may exceed 128)
+      // Pass 1: row max of the scaled scores.
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BKV; c += 32) {
+        float v[32];
+        tmem_ld32(t_s + lane_off + uint32_t(c), v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c + e < kvalid) mx = fmaxf(mx, v[e] * p.scale_log2);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = ex2f(m - m_new);  // 0 on the first tile (m = -inf)
+      // The previous P V^T has finished: O is stable and the P tile is free.
+      if (j > 0) {
+        if (!mbar_wait_idle(pv_done, (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+        tc_fence_after();
+        // Rescale O when the max grew for some row of this warp.
+        if (__any_sync(0xffffffffu, m_new > m)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            float o[32];
+            tmem_ld32(t_o + lane_off + uint32_t(c), o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(t_o + lane_off + uint32_t(c), o);
+          }
+        }
+      }
+      // Pass 2: P = exp2(s * scale_log2 - m_new) as bf16 into the swizzled
+      // A tile (row r: 128 keys = two 64-key atoms of 128 bytes), row sum.
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BKV; c += 32) {
+        float v[32];
+        tmem_ld32(t_s + lane_off + uint32_t(c), v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          v[e] = (c + e < kvalid) ? ex2f(v[e] * p.scale_log2 - m_new) : 0.f;
+          sum += v[e];
+        }
+        uint8_t* rowp = sp + (c >> 6) * (BQ * 128) + r * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = ((c & 63) >> 3) + q;
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = v[8 * q + e];
+          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) = pack(f, __nv_bfloat16());
+        }
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      // S has been read; P is in shared memory and O is rescaled.
+      tc_fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free);
+        mbar_arrive(p_full);
+      }
+    }
+    // Epilogue: O / l, bf16, after the last P V^T.
+    if (ok && nkv > 0 && mbar_wait_idle(pv_done, (nkv - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t qi = int64_t(q0) + r;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + int64_t(b) * p.ob +
+                            int64_t(h) * p.oh + qi * p.on;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        tmem_ld32(t_o + lane_off + uint32_t(c), o);
+        if (qi < p.nq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = o[8 * q + e] * inv;
+            *reinterpret_cast<uint4*>(orow + c + 8 * q) = pack(f, __nv_bfloat16());
+          }
+        }
+      }
+    }
+  }
+
+  // Teardown: MMAs complete before TMEM is released (bounded).
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 32) {
+    const uint64_t t1 = globaltimer();
+    while (globaltimer() - t1 < 1000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// v [B, H, nk, D] -> vt [B, H, D, ldk] (keys contiguous, zero past nk).
+__global__ void transpose_v_kernel(const __nv_bfloat16* __restrict__ v, int64_t sb, int64_t sh,
+                                   int64_t sn, int H, int64_t nk, int D, int64_t ldk,
+                                   __nv_bfloat16* __restrict__ vt) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int bh = blockIdx.z;
+  const int b = bh / H, h = bh - b * H;
+  const int64_t k0 = int64_t(blockIdx.x) * 32;
+  const int d0 = blockIdx.y * 32;
+  const __nv_bfloat16* vb = v + int64_t(b) * sb + int64_t(h) * sh;
+  __nv_bfloat16* ob = vt + int64_t(bh) * D * ldk;
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const int64_t key = k0 + y;
+    const int d = d0 + threadIdx.x;
+    tile[y][threadIdx.x] = (key < nk && d < D) ? vb[key * sn + d] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const int d = d0 + y;
+    const int64_t key = k0 + threadIdx.x;
+    if (d < D && key < ldk) ob[int64_t(d) * ldk + key] = tile[threadIdx.x][y];
+  }
+}
+
+// 4-D bf16 view [B, H, rows, cols] (cols contiguous) as a TMA map with a box
+// of 64 columns x box_rows rows, 128B swizzle.  The map's dimensions are
+// ordered by stride: (cols, rows, H, B), or (cols, H, rows, B) when heads are
+// closer in memory than rows (*hn = 1; the kernel swaps those coordinates).
+// Strides of size-1 dimensions are replaced by packed ones.
+static bool make_map4(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t rows,
+                      int64_t cols, int64_t s_row, int64_t s_h, int64_t s_b, uint32_t box_rows,
+                      int* hn) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if (rows <= 1) s_row = cols;
+  if (H <= 1) s_h = s_row * rows;
+  if (B <= 1) s_b = (s_h > s_row ? s_h * H : s_row * rows);
+  *hn = s_h < s_row ? 1 : 0;
+  const cuuint64_t dims[4] = {uint64_t(cols), uint64_t(*hn ? H : rows), uint64_t(*hn ? rows : H),
+                              uint64_t(B)};
+  const cuuint64_t strides[3] = {uint64_t(*hn ? s_h : s_row) * 2, uint64_t(*hn ? s_row : s_h) * 2,
+                                 uint64_t(s_b) * 2};
+  const cuuint32_t box[4] = {64u, *hn ? 1u : box_rows, *hn ? box_rows : 1u, 1u};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace attn
+}  // namespace l3d
+
+using namespace l3d;
+
+extern "C" size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk, int64_t d) {
+  if (b < 0 || h < 0 || nk < 0 || d < 0) return 0;
+  const int64_t ldk = (nk + 7) / 8 * 8;
+  return 256 + attn::align256(size_t(b) * size_t(h) * size_t(d) * size_t(ldk) * 2);
+}
+
+extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v,
+                             float scale, const l3d_tensor* out, void* workspace,
+                             size_t workspace_bytes, l3d_stream stream) {
+  const char* op = "l3d_attention";
+  using namespace l3d::attn;
+  const l3d_tensor* all[] = {q, k, v, out};
+  for (const l3d_tensor* t : all) {
+    if (!t) return fail(L3D_E_NULL, "%s: q, k, v and out are required", op);
+    if (t->dtype != L3D_BF16) return fail(L3D_E_DTYPE, "%s: q, k, v, out must be BF16", op);
+    if (t->ndim != 4) return fail(L3D_E_SHAPE, "%s: tensors must be [B, H, N, D]", op);
+    if (t->strides[3] != 1) return fail(L3D_E_ALIGN, "%s: the head dim must be contiguous", op);
+  }
+  const int64_t B = q->dims[0], H = q->dims[1], nq = q->dims[2], D = q->dims[3];
+  const int64_t nk = k->dims[2];
+  if (k->dims[0] != B || k->dims[1] != H || k->dims[3] != D || v->dims[0] != B ||
+      v->dims[1] != H || v->dims[2] != nk || v->dims[3] != D || out->dims[0] != B ||
+      out->dims[1] != H || out->dims[2] != nq || out->dims[3] != D)
+    return fail(L3D_E_SHAPE, "%s: q [B,H,N,D], k and v [B,H,Nk,D], out [B,H,N,D]", op);
+  if (D != 64 && D != 128) return fail(L3D_E_UNSUPPORTED, "%s: head dim must be 64 or 128", op);
+  if (B > 65535 || H > 65535 || nq > (int64_t(1) << 30) || nk > (int64_t(1) << 30))
+    return fail(L3D_E_UNSUPPORTED, "%s: dimensions too large", op);
+  const size_t need = l3d_attention_workspace_size(B, H, nk, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(L3D_E_ALIGN, "%s: workspace must be 256-byte aligned", op);
+  if (B * H * nq == 0) return L3D_OK;
+  for (const l3d_tensor* t : all) {
+    if (no_data(t)) return fail(L3D_E_NULL, "%s: null data pointer", op);
+    if (reinterpret_cast<uintptr_t>(elem_ptr(t)) % 16)
+      return fail(L3D_E_ALIGN, "%s: tensors must be 16-byte aligned", op);
+    for (int i = 0; i < 3; ++i)
+      if (t->dims[i] > 1 && (t->strides[i] * 2) % 16)
+        return fail(L3D_E_ALIGN, "%s: strides must be multiples of 16 bytes", op);
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  if (cudaMemsetAsync(status, 0, 256, s) != cudaSuccess)
+    return fail(L3D_E_CUDA, "%s: status clear failed", op);
+  if (nk == 0) {
+    // softmax over no keys: zeros, as an empty sum.
+    const int64_t on = out->strides[2];
+    if (on == D && out->strides[1] == nq * D && out->strides[0] == H * nq * D) {
+      if (cudaMemsetAsync(const_cast<char*>(elem_ptr(out)), 0, size_t(B * H * nq * D) * 2, s) !=
+          cudaSuccess)
+        return fail(L3D_E_CUDA, "%s: memset failed", op);
+      return L3D_OK;
+    }
+    return fail(L3D_E_UNSUPPORTED, "%s: empty keys need a contiguous out", op);
+  }
+  // V^T [B, H, D, ldk] in the workspace.
+  const int64_t ldk = (nk + 7) / 8 * 8;
+  __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+  {
+    const dim3 grid(unsigned((ldk + 31) / 32), unsigned((D + 31) / 32), unsigned(B * H));
+    transpose_v_kernel<<<grid, dim3(32, 8), 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(elem_ptr(v)), v->strides[0], v->strides[1],
+        v->strides[2], int(H), nk, int(D), ldk, vt);
+  }
+  CUtensorMap map_q, map_k, map_vt;
+  int q_hn = 0, k_hn = 0, v_hn = 0;
+  if (!make_map4(&map_q, elem_ptr(q), B, H, nq, D, q->strides[2], q->strides[1], q->strides[0], BQ,
+                 &q_hn) ||
+      !make_map4(&map_k, elem_ptr(k), B, H, nk, D, k->strides[2], k->strides[1], k->strides[0], BKV,
+                 &k_hn) ||
+      !make_map4(&map_vt, vt, B, H, D, ldk, ldk, D * ldk, H * D * ldk, uint32_t(D), &v_hn) || v_hn)
+    return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed", op);
+  Params p{};
+  p.q_hn = q_hn;
+  p.k_hn = k_hn;
+  p.nq = nq;
+  p.nk = nk;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = const_cast<char*>(elem_ptr(out));
+  p.ob = out->strides[0];
+  p.oh = out->strides[1];
+  p.on = out->strides[2];
+  p.status = status;
+  const dim3 grid(unsigned((nq + BQ - 1) / BQ), unsigned(H), unsigned(B));
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Cfg<64>::SMEM);
+    if (attr == cudaSuccess)
+      attr = cudaFuncSetAttribute(attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg<128>::SMEM);
+  });
+  if (attr != cudaSuccess) return fail(L3D_E_CUDA, "%s: cannot reserve shared memory", op);
+  if (D == 64) attn_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, s>>>(map_q, map_k, map_vt, p);
+  else attn_kernel<128><<<grid, THREADS, Cfg<128>::SMEM, s>>>(map_q, map_k, map_vt, p);
+  return check_launch(op);
+}

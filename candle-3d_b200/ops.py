@@ -426,3 +426,27 @@ class SparseConv3d:
              ref(desc(counts)), chp, ref(desc(self.weight)), ref(desc(self.bias)),
              ref(desc(out)), ws.data_ptr(), ws.numel(), _s(feats))
         return out
+
+
+_ATTN_WS = {}
+
+
+def attention(q, k, v, scale=None, out=None):
+    """exact_sdpa_heads (crate/runtime/attention_math.rs:199-259): softmax(q k^T
+    * scale) v on [B, H, N, D] bf16 views (D = 64 or 128), tcgen05 flash
+    attention.  `out` defaults to token-major [B, N, H, D] memory viewed as
+    [B, H, N, D], so out.transpose(1, 2).reshape(B, N, H * D) is a view."""
+    _check_cuda(q, k, v, out)
+    B, H, N, D = q.shape
+    if scale is None:
+        scale = D ** -0.5
+    if out is None:
+        out = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device).transpose(1, 2)
+    need = _lib.lib().l3d_attention_workspace_size(B, H, k.shape[2], D)
+    ws = _ATTN_WS.get(q.device)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
+        _ATTN_WS[q.device] = ws
+    call("l3d_attention", ref(desc(q)), ref(desc(k)), ref(desc(v)), float(scale), ref(desc(out)),
+         ws.data_ptr(), ws.numel(), _s(q))
+    return out

@@ -352,6 +352,23 @@ int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor* pair_src,
                             const l3d_tensor* bias, const l3d_tensor* out, void* workspace,
                             size_t workspace_bytes, l3d_stream stream);
 
+/* ---- next row: the attention core --------------------------------------------- */
+
+/* Workspace bytes for l3d_attention. */
+size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk, int64_t d);
+
+/* exact_sdpa_heads / exact_query_chunked_sdpa
+ * (crate/runtime/attention_math.rs:199-259), non-causal: out = softmax(q k^T *
+ * scale) v per (batch, head), on the tensor cores (tcgen05, TMEM, TMA; online
+ * softmax in f32, P rounded to bf16 for the second product).  q [B, H, N, D],
+ * k and v [B, H, Nk, D], out [B, H, N, D], BF16, D = 64 or 128, any strides
+ * with the head dim contiguous and 16-byte multiples elsewhere (e.g. views of
+ * a [B, N, 3, H, D] projection or token-major [B, N, H, D] memory).  The
+ * workspace holds V transposed and a status word. */
+int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v, float scale,
+                  const l3d_tensor* out, void* workspace, size_t workspace_bytes,
+                  l3d_stream stream);
+
 /* ---- GGUF tensor index (the on-disk format feeding a13) ------------------------ */
 
 /* One tensor of a GGUF file.  name points into the caller's buffer (not

@@ -1,0 +1,69 @@
+"""GPU parity: tcgen05 flash attention (exact_sdpa_heads,
+crate/runtime/attention_math.rs:199-259) against softmax(q k^T * scale) v in
+torch f32 on the same bf16 inputs.
+
+Numerics: S and the running O are f32 (tensor-core accumulation); P is
+rounded to bf16 for the second product and the output to bf16, so the
+bound is |err| <= 2e-2 * max(1, |ref|) (bf16 tolerance) with a relative-L2
+check of 1e-2."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, k, v, scale):
+    s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    return (s.softmax(-1) @ v.float())
+
+
+@pytest.mark.parametrize("B,H,N,NK,D,layout", [
+    (1, 2, 256, 256, 64, "bhnd"),       # whole tiles
+    (2, 3, 200, 333, 64, "bhnd"),       # ragged q and kv tails, Nk != N
+    (1, 16, 1374, 1374, 64, "qkv"),     # VGGT frame attention: views of [B, N, 3, H, D]
+    (1, 4, 300, 300, 128, "bhnd"),      # D = 128 (TripoSG / TRELLIS heads)
+    (1, 4, 190, 190, 64, "bnhd"),       # token-major q, k, v memory
+    (1, 1, 5, 7, 64, "bhnd"),           # tiny
+])
+def test_attention_matches_torch(ops, dev, B, H, N, NK, D, layout):
+    import torch
+
+    g = torch.Generator().manual_seed(N * 7 + D)
+    if layout == "qkv":
+        qkv = torch.randn(B, N, 3, H, D, generator=g).to(dev, torch.bfloat16).permute(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+    elif layout == "bnhd":
+        q = torch.randn(B, N, H, D, generator=g).to(dev, torch.bfloat16).transpose(1, 2)
+        k = torch.randn(B, NK, H, D, generator=g).to(dev, torch.bfloat16).transpose(1, 2)
+        v = torch.randn(B, NK, H, D, generator=g).to(dev, torch.bfloat16).transpose(1, 2)
+    else:
+        q = torch.randn(B, H, N, D, generator=g).to(dev, torch.bfloat16)
+        k = torch.randn(B, H, NK, D, generator=g).to(dev, torch.bfloat16)
+        v = torch.randn(B, H, NK, D, generator=g).to(dev, torch.bfloat16)
+    scale = D ** -0.5
+    out = ops.attention(q, k, v, scale)
+    torch.cuda.synchronize()
+    ws = ops._ATTN_WS[q.device]
+    assert ws[:4].view(torch.int32).item() == 0  # no bounded wait expired
+    ref = _ref(q, k, v, scale)
+    got = out.float()
+    err = (got - ref).abs()
+    assert torch.all(err <= 2e-2 * torch.clamp(ref.abs(), min=1.0)), f"max err {err.max().item():.3e}"
+    rel = (torch.linalg.norm(got - ref) / torch.linalg.norm(ref)).item()
+    assert rel < 1e-2, rel
+
+
+def test_attention_sharp_softmax(ops, dev):
+    """Scores of large magnitude (max changes across tiles): the running max /
+    rescale path."""
+    import torch
+
+    g = torch.Generator().manual_seed(5)
+    B, H, N, D = 1, 2, 640, 64
+    q = (4 * torch.randn(B, H, N, D, generator=g)).to(dev, torch.bfloat16)
+    k = (4 * torch.randn(B, H, N, D, generator=g)).to(dev, torch.bfloat16)
+    v = torch.randn(B, H, N, D, generator=g).to(dev, torch.bfloat16)
+    out = ops.attention(q, k, v, D ** -0.5)
+    ref = _ref(q, k, v, D ** -0.5)
+    rel = (torch.linalg.norm(out.float() - ref) / torch.linalg.norm(ref)).item()
+    assert rel < 1e-2, rel

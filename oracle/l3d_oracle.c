@@ -628,3 +628,41 @@ int orc_neighbor_pairs(const int32_t* coords, int64_t n, int32_t* pair_dest, int
   free(tab);
   return 0;
 }
+
+/* SparseConv3d::forward (crate/runtime/trellis2_sparse.rs:197-243): for each
+ * kernel offset k in 0..26, the neighbour pairs (dest i, src j) in ascending i
+ * (the lists orc_neighbor_pairs builds), product[p, o] = sum_c feats[j, c] *
+ * w27[k, o, c] (f32, c ascending), then out[i, :] += product[p, :]
+ * (index_add); finally + bias.  feats [n, cin], w27 [27, cout, cin], bias
+ * [cout] or NULL, out [n, cout]. */
+int orc_sparse_conv3d(const int32_t* coords, int64_t n, const float* feats, int64_t cin,
+                      const float* w27, int64_t cout, const float* bias, float* out) {
+  int32_t* dest = (int32_t*)malloc(sizeof(int32_t) * (size_t)(27 * (n > 0 ? n : 1)));
+  int32_t* src = (int32_t*)malloc(sizeof(int32_t) * (size_t)(27 * (n > 0 ? n : 1)));
+  int32_t counts[27];
+  if (!dest || !src) { free(dest); free(src); return 1; }
+  orc_neighbor_pairs(coords, n, dest, src, counts);
+  for (int64_t i = 0; i < n * cout; ++i) out[i] = 0.f;
+  for (int k = 0; k < 27; ++k) {
+    const int32_t* dk = dest + (int64_t)k * n;
+    const int32_t* sk = src + (int64_t)k * n;
+    const float* wk = w27 + (int64_t)k * cout * cin;
+#pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < counts[k]; ++p) {
+      const float* x = feats + (int64_t)sk[p] * cin;
+      float* o = out + (int64_t)dk[p] * cout;
+      for (int64_t oc = 0; oc < cout; ++oc) {
+        const float* w = wk + oc * cin;
+        float acc = 0.f;
+        for (int64_t c = 0; c < cin; ++c) acc += x[c] * w[c];
+        o[oc] += acc;
+      }
+    }
+  }
+  if (bias)
+    for (int64_t i = 0; i < n; ++i)
+      for (int64_t oc = 0; oc < cout; ++oc) out[i * cout + oc] += bias[oc];
+  free(dest);
+  free(src);
+  return 0;
+}

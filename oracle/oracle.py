@@ -53,6 +53,7 @@ def lib():
         L = C.CDLL(str(LIB))
         sig = {
             "orc_round_array": [_f32p, _i64, _int],
+            "orc_sparse_conv3d": [C.c_void_p, _i64, _f32p, _i64, _f32p, _i64, C.c_void_p, _f32p],
             "orc_num_threads": [],
             "orc_set_num_threads": [_int],
             "orc_layer_norm": [_f32p, _i64, _i64, C.c_void_p, C.c_void_p, _flt, _f32p, _int],
@@ -346,6 +347,21 @@ def neighbor_pairs(coords):
 def kernel_offset_delta(k: int):
     """crate/runtime/trellis2_sparse.rs:99-106."""
     return (k // 9 - 1, (k % 9) // 3 - 1, k % 3 - 1)
+
+
+def sparse_conv3d(coords, feats, w27, bias=None):
+    """SparseConv3d::forward in f32: coords [N, 3] int, feats [N, Cin],
+    w27 [27, Cout, Cin], bias [Cout] or None -> [N, Cout]."""
+    c = _c(coords, np.int32)
+    f = _c(feats)
+    w = _c(w27)
+    n, cin = f.shape
+    cout = w.shape[1]
+    b = None if bias is None else _c(bias)
+    out = np.empty((n, cout), np.float32)
+    _chk(lib().orc_sparse_conv3d(c.ctypes.data, n, f, cin, w, cout,
+                                 None if b is None else b.ctypes.data, out), "sparse_conv3d")
+    return out
 
 
 if __name__ == "__main__":

@@ -12,10 +12,12 @@
 //   warp 1     MMA issuer: S = Q K^T (M 128, N 128, K D) into TMEM, then
 //              O += P V^T (M 128, N D, K 128) once P is ready;
 //   warps 2-5  softmax / epilogue, one query row per thread (its TMEM lane):
-//              pass 1 reads S and forms the row max, the running O is rescaled
-//              in TMEM when the max grows, pass 2 writes P = exp2(S * scale
-//              * log2 e - m) as bf16 into the 128B-swizzled operand tile and
-//              accumulates the row sum; after the last tile O / l is stored.
+//              the row of S is copied to registers (S is released at once, so
+//              the next S = Q K^T overlaps the exponentials), the running O
+//              is rescaled in TMEM when the max grows, P = exp2(S * scale *
+//              log2 e - m) is written as bf16 into the 128B-swizzled operand
+//              tile and the row sum accumulated; after the last tile O / l is
+//              stored.
 // TMEM: S in columns [0, 128), O in [128, 128 + D) - 256 columns, so two CTAs
 // share an SM.  Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry
 // the CTA records an error in the workspace status word and stops.
@@ -31,6 +33,7 @@ constexpr int BQ = 128, BKV = 128;
 constexpr int THREADS = 6 * 32;
 constexpr int TMEM_COLS = 256;
 constexpr int ST_TIMEOUT = 5;
+constexpr int ST_MISALIGNED = 6;
 
 template <int D>
 struct Cfg {
@@ -40,7 +43,10 @@ struct Cfg {
   static constexpr int V_BYTES = D * BKV * 2;         // V^T tile: D rows x 128 keys
   static constexpr int P_BYTES = BQ * BKV * 2;
   static constexpr int STAGES = 2;
-  static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 1024 + 256;
+  // No alignment slack: with no static shared memory the dynamic window
+  // starts 1024-byte aligned (checked at run time), and for D = 64 two CTAs
+  // then fit on one SM.
+  static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 256;
   static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
   static constexpr uint32_t IDESC_O = make_idesc(128, D);
 };
@@ -97,8 +103,12 @@ __global__ void __launch_bounds__(THREADS, 2)
                 const __grid_constant__ CUtensorMap map_vt, const Params p) {
   using C = Cfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  // The swizzled tiles need 1024-byte alignment; report and stop otherwise.
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, ST_MISALIGNED);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sq = smem;                                  // [DC][128 x 64]
   uint8_t* sk = sq + C::Q_BYTES;                       // [STAGES][DC][128 x 64]
   uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][2][D x 64]
@@ -168,14 +178,11 @@ __global__ void __launch_bounds__(THREADS, 2)
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, ST_TIMEOUT)) break;
-        // S is free once the softmax warps have read the previous tile's S.
-        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) break;
-        tc_fence_after();
-        const uint8_t* kt = sk + s * C::K_BYTES;
+      // S(j + 1) is issued as soon as the softmax warps have copied S(j) to
+      // registers, so it overlaps their exponentials; O += P(j) V(j)^T
+      // follows once P(j) is written.
+      auto issue_s = [&](int j) {
+        const uint8_t* kt = sk + (j & 1) * C::K_BYTES;
 #pragma unroll
         for (int dc = 0; dc < C::DC; ++dc) {
           const uint64_t da = smem_desc_sw128(sq + dc * (BQ * 128));
@@ -185,6 +192,22 @@ __global__ void __launch_bounds__(THREADS, 2)
             umma_f16<C::IDESC_S>(t_s, da + uint64_t(2 * k), db + uint64_t(2 * k), (dc | k) ? 1u : 0u);
         }
         umma_commit(s_full);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT) &&
+                mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int s = j & 1;
+        if (j + 1 < nkv) {
+          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, ST_TIMEOUT) ||
+              !mbar_wait(s_free, j & 1, abort_flag, p.status, ST_TIMEOUT))
+            break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
         // O += P V^T once the softmax warps have written P (and rescaled O).
         if (!mbar_wait(p_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) break;
         tc_fence_after();
@@ -213,15 +236,19 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (!mbar_wait_idle(s_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
       tc_fence_after();
       const int kvalid = int(p.nk - int64_t(j) * BKV);  // keys of this tile (may exceed 128)
-      // Pass 1: row max of the scaled scores.
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BKV; c += 32) {
-        float v[32];
-        tmem_ld32(t_s + lane_off + uint32_t(c), v);
+      // The row's 128 scores into registers; S is then free for S(j + 1).
+      float sv[BKV];
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c + e < kvalid) mx = fmaxf(mx, v[e] * p.scale_log2);
+      for (int c = 0; c < BKV; c += 32)
+        tmem_ld32(t_s + lane_off + uint32_t(c), *reinterpret_cast<float(*)[32]>(&sv[c]));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BKV; ++e) {
+        sv[e] = (e < kvalid) ? sv[e] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[e]);
       }
       const float m_new = fmaxf(m, mx);
       const float alpha = ex2f(m - m_new);  // 0 on the first tile (m = -inf)
@@ -241,38 +268,28 @@ __global__ void __launch_bounds__(THREADS, 2)
           }
         }
       }
-      // Pass 2: P = exp2(s * scale_log2 - m_new) as bf16 into the swizzled
-      // A tile (row r: 128 keys = two 64-key atoms of 128 bytes), row sum.
+      // P = exp2(s - m_new) as bf16 into the swizzled A tile (row r: 128 keys
+      // = two 64-key atoms of 128 bytes), and the row sum.
       float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < BKV; c += 32) {
-        float v[32];
-        tmem_ld32(t_s + lane_off + uint32_t(c), v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          v[e] = (c + e < kvalid) ? ex2f(v[e] * p.scale_log2 - m_new) : 0.f;
-          sum += v[e];
+      for (int c = 0; c < BKV; c += 8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          f[e] = ex2f(sv[c + e] - m_new);
+          sum += f[e];
         }
         uint8_t* rowp = sp + (c >> 6) * (BQ * 128) + r * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = ((c & 63) >> 3) + q;
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = v[8 * q + e];
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) = pack(f, __nv_bfloat16());
-        }
+        const int chunk = (c & 63) >> 3;
+        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) = pack(f, __nv_bfloat16());
       }
       l = l * alpha + sum;
       m = m_new;
-      // S has been read; P is in shared memory and O is rescaled.
+      // P is in shared memory and O is rescaled.
       tc_fence_before();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(p_full);
     }
     // Epilogue: O / l, bf16, after the last P V^T.
     if (ok && nkv > 0 && mbar_wait_idle(pv_done, (nkv - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) {

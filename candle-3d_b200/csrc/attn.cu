@@ -6,11 +6,11 @@
 //
 // One CTA per (128-query tile, head, batch), 6 warps:
 //   warp 0     TMA producer: the Q tile once, then a 2-stage ring of K tiles
-//              (128 keys x D) and V^T tiles (D x 128 keys; V is transposed
+//              (BKV keys x D) and V^T tiles (D x BKV keys; V is transposed
 //              once per call into the workspace so that both products take
-//              K-major operands);
-//   warp 1     MMA issuer: S = Q K^T (M 128, N 128, K D) into TMEM, then
-//              O += P V^T (M 128, N D, K 128) once P is ready;
+//              K-major operands); BKV = 128 for D = 64, 64 for D = 128;
+//   warp 1     MMA issuer: S = Q K^T (M 128, N BKV, K D) into TMEM, then
+//              O += P V^T (M 128, N D, K BKV) once P is ready;
 //   warps 2-5  softmax / epilogue, one query row per thread (its TMEM lane):
 //              the row of S is copied to registers (S is released at once, so
 //              the next S = Q K^T overlaps the exponentials), the running O
@@ -18,8 +18,8 @@
 //              log2 e - m) is written as bf16 into the 128B-swizzled operand
 //              tile and the row sum accumulated; after the last tile O / l is
 //              stored.
-// TMEM: S in columns [0, 128), O in [128, 128 + D) - 256 columns, so two CTAs
-// share an SM.  Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry
+// TMEM: S in columns [0, BKV), O in [128, 128 + D) - 256 columns; with under
+// half an SM of shared memory per CTA, two CTAs share an SM.  Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry
 // the CTA records an error in the workspace status word and stops.
 #include "common.cuh"
 #include "tc.cuh"
@@ -29,23 +29,31 @@ namespace attn {
 
 using namespace l3d::tc;
 
-constexpr int BQ = 128, BKV = 128;
+constexpr int BQ = 128;
 constexpr int THREADS = 6 * 32;
-constexpr int TMEM_COLS = 256;
+constexpr int TMEM_COLS = 256;  // S in [0, BKV), O in [128, 128 + D)
 constexpr int ST_TIMEOUT = 5;
 constexpr int ST_MISALIGNED = 6;
+// The running max moves only when a row's max grows by more than 2^8 (log2
+// units): until then exp2(s - m) <= 256, and O and l share the stale max, so
+// the result is unchanged while most O rescales are skipped.
+constexpr float RESCALE_LOG2 = 8.f;
 
+// Key tile: 128 keys for D = 64, 64 for D = 128, so that the shared memory of
+// one CTA stays below half an SM in both cases (two CTAs per SM alternate
+// between softmax and MMA).
 template <int D>
 struct Cfg {
+  static constexpr int BKV = D == 64 ? 128 : 64;
   static constexpr int DC = D / 64;                   // 64-wide K atoms of Q / K
+  static constexpr int KA = BKV / 64;                 // 64-key atoms of P / V^T
   static constexpr int Q_BYTES = BQ * D * 2;
   static constexpr int K_BYTES = BKV * D * 2;
-  static constexpr int V_BYTES = D * BKV * 2;         // V^T tile: D rows x 128 keys
+  static constexpr int V_BYTES = D * BKV * 2;         // V^T tile: D rows x BKV keys
   static constexpr int P_BYTES = BQ * BKV * 2;
   static constexpr int STAGES = 2;
   // No alignment slack: with no static shared memory the dynamic window
-  // starts 1024-byte aligned (checked at run time), and for D = 64 two CTAs
-  // then fit on one SM.
+  // starts 1024-byte aligned (checked at run time).
   static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 256;
   static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
   static constexpr uint32_t IDESC_O = make_idesc(128, D);
@@ -54,7 +62,7 @@ struct Cfg {
 struct Params {
   int64_t nq, nk;       // query / key lengths
   int q_hn, k_hn;       // the q / k maps list heads before rows (token-major memory)
-  float scale_log2;     // softmax scale * log2(e)
+  float scale_log2;     // softmax scale * log2(e), > 0
   void* out;            // [B, H, nq, D] bf16
   int64_t ob, oh, on;   // out strides (elements)
   int* status;
@@ -68,6 +76,34 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+
+// 64 consecutive f32 TMEM columns of this thread's lane -> registers; the
+// wait is inside the same statement, so no use can move above it.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, "
+      "%45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, "
+      "%62, %63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]),
+        "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]),
+        "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
+        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]),
+        "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]),
+        "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // 32 consecutive f32 TMEM columns of this thread's lane <- registers.
@@ -102,6 +138,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_vt, const Params p) {
   using C = Cfg<D>;
+  constexpr int BKV = C::BKV;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The swizzled tiles need 1024-byte alignment; report and stop otherwise.
   if (smem_u32(smem_raw) & 1023u) {
@@ -110,9 +147,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
   uint8_t* smem = smem_raw;
   uint8_t* sq = smem;                                  // [DC][128 x 64]
-  uint8_t* sk = sq + C::Q_BYTES;                       // [STAGES][DC][128 x 64]
-  uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][2][D x 64]
-  uint8_t* sp = sv + C::STAGES * C::V_BYTES;           // [2][128 x 64]
+  uint8_t* sk = sq + C::Q_BYTES;                       // [STAGES][DC][BKV x 64]
+  uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][KA][D x 64]
+  uint8_t* sp = sv + C::STAGES * C::V_BYTES;           // [KA][128 x 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sp + C::P_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;        // [STAGES]
@@ -151,7 +188,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t t_s = tmem_base, t_o = tmem_base + BKV;
+  const uint32_t t_s = tmem_base, t_o = tmem_base + 128;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -171,7 +208,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           tma_load_4d(kt + dc * (BKV * 128), &map_k, &kv_full[s], dc * 64, p.k_hn ? h : j * BKV,
                       p.k_hn ? j * BKV : h, b);
         uint8_t* vt = sv + s * C::V_BYTES;
-        for (int kc = 0; kc < 2; ++kc)
+        for (int kc = 0; kc < C::KA; ++kc)
           tma_load_4d(vt + kc * (D * 128), &map_vt, &kv_full[s], j * BKV + kc * 64, 0, h, b);
       }
     }
@@ -213,7 +250,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         tc_fence_after();
         const uint8_t* vt = sv + s * C::V_BYTES;
 #pragma unroll
-        for (int kc = 0; kc < 2; ++kc) {
+        for (int kc = 0; kc < C::KA; ++kc) {
           const uint64_t da = smem_desc_sw128(sp + kc * (BQ * 128));
           const uint64_t db = smem_desc_sw128(vt + kc * (D * 128));
 #pragma unroll
@@ -230,60 +267,73 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;           // query row within the tile
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    float m = -INFINITY, l = 0.f;
+    const float2 sc2 = f2(p.scale_log2);
+    float m = -INFINITY;                         // running max, log2 units
+    float2 l2 = f2(0.f);                         // running row sum (two halves)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait_idle(s_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
       tc_fence_after();
-      const int kvalid = int(p.nk - int64_t(j) * BKV);  // keys of this tile (may exceed 128)
-      // The row's 128 scores into registers; S is then free for S(j + 1).
+      // The row's scores into registers; S is then free for S(j + 1).
       float sv[BKV];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 32)
-        tmem_ld32(t_s + lane_off + uint32_t(c), *reinterpret_cast<float(*)[32]>(&sv[c]));
+      for (int c = 0; c < BKV; c += 64) tmem_ld64(t_s + lane_off + uint32_t(c), sv + c);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
-      float mx = -INFINITY;
+      const int kvalid = int(p.nk - int64_t(j) * BKV);  // keys of this tile (may exceed BKV)
+      if (kvalid < BKV) {
 #pragma unroll
-      for (int e = 0; e < BKV; ++e) {
-        sv[e] = (e < kvalid) ? sv[e] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[e]);
+        for (int e = 0; e < BKV; ++e)
+          if (e >= kvalid) sv[e] = -INFINITY;
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = ex2f(m - m_new);  // 0 on the first tile (m = -inf)
+      float mx0 = sv[0], mx1 = sv[1];
+#pragma unroll
+      for (int e = 2; e < BKV; e += 2) {
+        mx0 = fmaxf(mx0, sv[e]);
+        mx1 = fmaxf(mx1, sv[e + 1]);
+      }
+      const float mxs = fmaxf(mx0, mx1) * p.scale_log2;  // scale > 0
+      const bool grow = mxs > m + RESCALE_LOG2;          // always on the first tile
+      const float m_new = grow ? mxs : m;
+      const float alpha = grow ? ex2f(m - m_new) : 1.f;  // 0 on the first tile
       // The previous P V^T has finished: O is stable and the P tile is free.
       if (j > 0) {
         if (!mbar_wait_idle(pv_done, (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
         tc_fence_after();
-        // Rescale O when the max grew for some row of this warp.
-        if (__any_sync(0xffffffffu, m_new > m)) {
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             float o[32];
             tmem_ld32(t_o + lane_off + uint32_t(c), o);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            for (int e = 0; e < 32; e += 2) {
+              const float2 v = mul2(make_float2(o[e], o[e + 1]), f2(alpha));
+              o[e] = v.x;
+              o[e + 1] = v.y;
+            }
             tmem_st32(t_o + lane_off + uint32_t(c), o);
           }
         }
       }
-      // P = exp2(s - m_new) as bf16 into the swizzled A tile (row r: 128 keys
-      // = two 64-key atoms of 128 bytes), and the row sum.
-      float sum = 0.f;
+      // P = exp2(s * scale * log2 e - m) as bf16 into the swizzled A tile
+      // (row r: BKV keys = 64-key atoms of 128 bytes), and the row sum.
+      const float2 nm2 = f2(-m_new);
+      l2 = mul2(l2, f2(alpha));
 #pragma unroll
       for (int c = 0; c < BKV; c += 8) {
         float f[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          f[e] = ex2f(sv[c + e] - m_new);
-          sum += f[e];
+        for (int e = 0; e < 8; e += 2) {
+          const float2 x = fma2(make_float2(sv[c + e], sv[c + e + 1]), sc2, nm2);
+          f[e] = ex2f(x.x);
+          f[e + 1] = ex2f(x.y);
+          l2 = add2(l2, make_float2(f[e], f[e + 1]));
         }
         uint8_t* rowp = sp + (c >> 6) * (BQ * 128) + r * 128;
         const int chunk = (c & 63) >> 3;
         *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) = pack(f, __nv_bfloat16());
       }
-      l = l * alpha + sum;
       m = m_new;
       // P is in shared memory and O is rescaled.
       tc_fence_before();
@@ -294,6 +344,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     // Epilogue: O / l, bf16, after the last P V^T.
     if (ok && nkv > 0 && mbar_wait_idle(pv_done, (nkv - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) {
       tc_fence_after();
+      const float l = l2.x + l2.y;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int64_t qi = int64_t(q0) + r;
       __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + int64_t(b) * p.ob +
@@ -412,6 +463,8 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
       out->dims[1] != H || out->dims[2] != nq || out->dims[3] != D)
     return fail(L3D_E_SHAPE, "%s: q [B,H,N,D], k and v [B,H,Nk,D], out [B,H,N,D]", op);
   if (D != 64 && D != 128) return fail(L3D_E_UNSUPPORTED, "%s: head dim must be 64 or 128", op);
+  if (!(scale > 0.f) || !(scale < 3.0e38f))
+    return fail(L3D_E_UNSUPPORTED, "%s: scale must be positive and finite", op);
   if (B > 65535 || H > 65535 || nq > (int64_t(1) << 30) || nk > (int64_t(1) << 30))
     return fail(L3D_E_UNSUPPORTED, "%s: dimensions too large", op);
   const size_t need = l3d_attention_workspace_size(B, H, nk, D);
@@ -457,8 +510,8 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
   int q_hn = 0, k_hn = 0, v_hn = 0;
   if (!make_map4(&map_q, elem_ptr(q), B, H, nq, D, q->strides[2], q->strides[1], q->strides[0], BQ,
                  &q_hn) ||
-      !make_map4(&map_k, elem_ptr(k), B, H, nk, D, k->strides[2], k->strides[1], k->strides[0], BKV,
-                 &k_hn) ||
+      !make_map4(&map_k, elem_ptr(k), B, H, nk, D, k->strides[2], k->strides[1], k->strides[0],
+                 uint32_t(D == 64 ? Cfg<64>::BKV : Cfg<128>::BKV), &k_hn) ||
       !make_map4(&map_vt, vt, B, H, D, ldk, ldk, D * ldk, H * D * ldk, uint32_t(D), &v_hn) || v_hn)
     return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed", op);
   Params p{};

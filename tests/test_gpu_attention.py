@@ -67,3 +67,38 @@ def test_attention_sharp_softmax(ops, dev):
     ref = _ref(q, k, v, D ** -0.5)
     rel = (torch.linalg.norm(out.float() - ref) / torch.linalg.norm(ref)).item()
     assert rel < 1e-2, rel
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("span", [12.0, 60.0])
+def test_attention_rising_scores(ops, dev, D, span):
+    """Scores that rise along the keys by `span` (natural-log units) over the
+    sequence: the row max grows tile after tile, sometimes by less than the
+    rescale threshold (O keeps the stale max) and sometimes by more."""
+    import torch
+
+    g = torch.Generator().manual_seed(D + int(span))
+    B, H, N, NK = 1, 2, 300, 700
+    u = torch.randn(D, generator=g)
+    u = u / u.norm()
+    q = (u * D ** 0.5).expand(B, H, N, D).contiguous()
+    ramp = torch.linspace(0, span, NK)[:, None] * u + 0.05 * torch.randn(NK, D, generator=g)
+    k = ramp.expand(B, H, NK, D).contiguous()
+    v = torch.randn(B, H, NK, D, generator=g)
+    q, k, v = (t.to(dev, torch.bfloat16) for t in (q, k, v))
+    out = ops.attention(q, k, v, D ** -0.5)
+    torch.cuda.synchronize()
+    assert ops._ATTN_WS[q.device][:4].view(torch.int32).item() == 0
+    ref = _ref(q, k, v, D ** -0.5)
+    err = (out.float() - ref).abs()
+    assert torch.all(err <= 2e-2 * torch.clamp(ref.abs(), min=1.0)), f"max err {err.max().item():.3e}"
+    rel = (torch.linalg.norm(out.float() - ref) / torch.linalg.norm(ref)).item()
+    assert rel < 1e-2, rel
+
+
+def test_attention_rejects_bad_scale(ops, dev):
+    import torch
+
+    q = torch.zeros(1, 1, 8, 64, device=dev, dtype=torch.bfloat16)
+    with pytest.raises(Exception, match="scale"):
+        ops.attention(q, q, q, -1.0)

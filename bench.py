@@ -52,11 +52,15 @@ def parse():
     ap.add_argument("--qfmt", default="q8_0", choices=["q8_0", "q4_k", "q5_k", "q6_k"],
                     help="qlinear workload: weight format (q8_0 is config 4's)")
     ap.add_argument("--workload", default="chain",
-                    choices=["chain", "vggt", "triposg", "trellis", "qlinear", "sparseconv"],
+                    choices=["chain", "vggt", "triposg", "trellis", "qlinear", "sparseconv",
+                             "attention"],
                     help="chain: config 5 fused layer-op chain (GB/s); vggt / triposg / "
                          "trellis: config 2 / 3 / 4 block stacks (tokens/s); qlinear: the four "
                          "Q8_0 linears of one config-4 block (TFLOP/s); sparseconv: the "
-                         "TRELLIS.2 VAE's first submanifold conv (TFLOP/s)")
+                         "TRELLIS.2 VAE's first submanifold conv (TFLOP/s); attention: "
+                         "the attention core of one block (TFLOP/s, --attn-case)")
+    ap.add_argument("--attn-case", default="vggt-global", choices=list(ATTN_CASES),
+                    help="attention workload: which block's attention (B, H, N, D)")
     ap.add_argument("--conv-channels", type=int, default=1024,
                     help="sparseconv workload: Cin = Cout (1024 is the VAE's first stage)")
     return ap.parse_args()
@@ -367,6 +371,77 @@ def run_vggt(args, world, rank, local):
     return 0
 
 
+# (B, H, N, D) of the attention cores in the block stacks: VGGT frame (8 frames
+# of 1374 tokens) and global (8 x 1374 tokens), TRELLIS SLAT self-attention
+# (~31.5k voxels, 12 heads of 128), TripoSG self-attention (CFG batch 2, 2049
+# tokens, 16 heads of 128).
+ATTN_CASES = {"vggt-frame": (8, 16, 1374, 64), "vggt-global": (1, 16, 10992, 64),
+              "trellis": (1, 12, 31569, 128), "triposg": (2, 16, 2049, 128)}
+
+
+def run_attention(args, local):
+    """The attention core (exact_sdpa_heads) of one block: q, k, v as views
+    of token-major [B, N, H, D] bf16 memory, as the block stacks lay them out.
+    One step = one call.  FLOPs counted: 4 * B * H * N^2 * D (two products).
+    torch's scaled_dot_product_attention on the same views is timed beside it
+    (sdpa_ms), as the library comparison."""
+    import torch
+    import torch.nn.functional as F
+
+    import __graft_entry__ as graft
+
+    graft.load_package()
+    from candle3d_b200 import ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, H, N, D = ATTN_CASES[args.attn_case]
+    g = torch.Generator().manual_seed(20261202)
+    q, k, v = (torch.randn(B, N, H, D, generator=g).to(dev, torch.bfloat16).transpose(1, 2)
+               for _ in range(3))
+    out = torch.empty(B, N, H, D, device=dev, dtype=torch.bfloat16).transpose(1, 2)
+    flops = 4.0 * B * H * N * N * D
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, steps):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    ms_sdpa = timed(lambda: F.scaled_dot_product_attention(q, k, v), 5) / 5
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms = timed(lambda: ops.attention(q, k, v, D ** -0.5, out=out), args.steps)
+    clocks = sampler.stop()
+    tf = flops * args.steps / (ms / 1e3) / 1e12
+    peak = 1641.7
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak = float(json.loads(pk.read_text()).get("bf16_tflops", peak))
+    print(json.dumps({
+        "metric": "attention TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": f"attention core, {args.attn_case}: B={B} H={H} N={N} D={D}, "
+                               "q/k/v views of token-major memory",
+                   "baseline_metric": BASELINE_METRIC},
+        "roofline": {"bound": "tensor", "kernel": f"attn_kernel<{D}>", "achieved": round(tf, 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4), "traffic": None},
+        "sdpa_ms": round(ms_sdpa, 4),
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+    }))
+    return 0
+
+
 def run_sparseconv(args, local):
     """The submanifold sparse conv 3x3x3 (SparseConv3d::forward) of the
     TRELLIS.2 VAE's first stage: Cin = Cout = --conv-channels on the config-4
@@ -606,6 +681,8 @@ def main():
             return run_qlinear(args, local)
         if args.workload == "sparseconv":
             return run_sparseconv(args, local)
+        if args.workload == "attention":
+            return run_attention(args, local)
         return run_dit(args, local)
     C, T = args.channels, args.rows
     H, D, kind = head_cfg(C)

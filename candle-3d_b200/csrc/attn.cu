@@ -4,23 +4,31 @@
 //
 //   out[b, h, i, :] = softmax_j(q[b,h,i,:] . k[b,h,j,:] * scale) v[b,h,j,:]
 //
-// One CTA per (128-query tile, head, batch), 6 warps:
-//   warp 0     TMA producer: the Q tile once, then a 2-stage ring of K tiles
-//              (BKV keys x D) and V^T tiles (D x BKV keys; V is transposed
-//              once per call into the workspace so that both products take
-//              K-major operands); BKV = 128 for D = 64, 64 for D = 128;
-//   warp 1     MMA issuer: S = Q K^T (M 128, N BKV, K D) into TMEM, then
-//              O += P V^T (M 128, N D, K BKV) once P is ready;
-//   warps 2-5  softmax / epilogue, one query row per thread (its TMEM lane):
-//              the row of S is copied to registers (S is released at once, so
-//              the next S = Q K^T overlaps the exponentials), the running O
-//              is rescaled in TMEM when the max grows, P = exp2(S * scale *
-//              log2 e - m) is written as bf16 into the 128B-swizzled operand
-//              tile and the row sum accumulated; after the last tile O / l is
-//              stored.
-// TMEM: S in columns [0, BKV), O in [128, 128 + D) - 256 columns; with under
-// half an SM of shared memory per CTA, two CTAs share an SM.  Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry
-// the CTA records an error in the workspace status word and stops.
+// One CTA per (256 queries = two 128-row tiles, head, batch), 10 warps, one
+// CTA per SM:
+//   warp 0     TMA producer: both Q tiles once, then a ring of K tiles (128
+//              keys x D) and V^T tiles (D x 128 keys; V is transposed once
+//              per call into the workspace so that both products take K-major
+//              operands);
+//   warp 1     MMA issuer.  Per key tile j and query tile t: O_t += P_t(j)
+//              V(j)^T (M 128, N D, K 128, P_t read from tensor memory) as soon
+//              as the softmax warps of t have written P_t(j), then S_t(j+1) =
+//              Q_t K(j+1)^T (M 128, N 128, K D, operands in shared memory).
+//              The two query tiles share each K / V load and alternate: while
+//              one tile's softmax runs, the tensor core works for the other;
+//   warps 2-9  softmax / epilogue, warps 2-5 for tile 0 and 6-9 for tile 1,
+//              one query row per thread (its TMEM lane): the row of S_t(j) is
+//              copied to registers, the running O_t is rescaled in TMEM when
+//              the max grows past the threshold, P = exp2(S * scale * log2 e
+//              - m) is stored to TMEM as packed bf16 over the first half of
+//              S_t's columns and the row sum accumulated; after the last tile
+//              O / l is stored.
+// Each tcgen05.commit tracks every MMA issued before it, and the MMAs of one
+// thread run in issue order, so "S_t(j+1) complete" also means that P_t(j) has
+// been consumed and O_t is stable: the softmax warps wait on one barrier per
+// tile.  TMEM (512 columns): S_0 / P_0, S_1 / P_1 (128 each), O_0, O_1 (D each).
+// Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry the CTA
+// records an error in the workspace status word and stops.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -29,9 +37,10 @@ namespace attn {
 
 using namespace l3d::tc;
 
-constexpr int BQ = 128;
-constexpr int THREADS = 6 * 32;
-constexpr int TMEM_COLS = 256;  // S in [0, BKV), O in [128, 128 + D)
+constexpr int BQ = 128;               // rows of one query tile
+constexpr int NT = 2;                  // query tiles per CTA
+constexpr int THREADS = (2 + 4 * NT) * 32;
+constexpr int TMEM_COLS = 512;
 constexpr int ST_TIMEOUT = 5;
 constexpr int ST_MISALIGNED = 6;
 // The running max moves only when a row's max grows by more than 2^8 (log2
@@ -39,24 +48,24 @@ constexpr int ST_MISALIGNED = 6;
 // the result is unchanged while most O rescales are skipped.
 constexpr float RESCALE_LOG2 = 8.f;
 
-// Key tile: 128 keys for D = 64, 64 for D = 128, so that the shared memory of
-// one CTA stays below half an SM in both cases (two CTAs per SM alternate
-// between softmax and MMA).
 template <int D>
 struct Cfg {
-  static constexpr int BKV = D == 64 ? 128 : 64;
+  static constexpr int BKV = 128;
   static constexpr int DC = D / 64;                   // 64-wide K atoms of Q / K
-  static constexpr int KA = BKV / 64;                 // 64-key atoms of P / V^T
-  static constexpr int Q_BYTES = BQ * D * 2;
+  static constexpr int KA = BKV / 64;                 // 64-key atoms of V^T
+  static constexpr int Q_BYTES = BQ * D * 2;          // one query tile
   static constexpr int K_BYTES = BKV * D * 2;
   static constexpr int V_BYTES = D * BKV * 2;         // V^T tile: D rows x BKV keys
-  static constexpr int P_BYTES = BQ * BKV * 2;
-  static constexpr int STAGES = 2;
+  static constexpr int STAGES = D == 64 ? 4 : 2;
   // No alignment slack: with no static shared memory the dynamic window
   // starts 1024-byte aligned (checked at run time).
-  static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 256;
+  static constexpr int SMEM = NT * Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 256;
   static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
   static constexpr uint32_t IDESC_O = make_idesc(128, D);
+  // TMEM columns (P_t over the first half of S_t)
+  static constexpr uint32_t COL_S = 0, COL_O = 2 * BKV;
+  static_assert(COL_O + 2 * D <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct Params {
@@ -76,6 +85,19 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M 128 x K 16, bf16 pairs packed in 32-bit
+// columns, rows = TMEM lanes) from tensor memory, B from a shared-memory
+// descriptor.
+template <uint32_t IDESC_>
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(IDESC_), "r"(accumulate));
 }
 
 // 64 consecutive f32 TMEM columns of this thread's lane -> registers; the
@@ -106,24 +128,21 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 32 consecutive f32 TMEM columns of this thread's lane <- registers.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+// 32 consecutive 32-bit TMEM columns of this thread's lane <- registers.
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
       "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
       "%28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
@@ -133,8 +152,14 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
+// Two floats -> packed bf16 pair (lo = a, the lower K index).
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 template <int D>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_vt, const Params p) {
   using C = Cfg<D>;
@@ -145,24 +170,21 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (threadIdx.x == 0) atomicCAS(p.status, 0, ST_MISALIGNED);
     return;
   }
-  uint8_t* smem = smem_raw;
-  uint8_t* sq = smem;                                  // [DC][128 x 64]
-  uint8_t* sk = sq + C::Q_BYTES;                       // [STAGES][DC][BKV x 64]
+  uint8_t* sq = smem_raw;                              // [NT][DC][128 x 64]
+  uint8_t* sk = sq + NT * C::Q_BYTES;                  // [STAGES][DC][BKV x 64]
   uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][KA][D x 64]
-  uint8_t* sp = sv + C::STAGES * C::V_BYTES;           // [KA][128 x 64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + C::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + C::STAGES * C::V_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;        // [STAGES]
-  uint64_t* kv_empty = bars + 3;       // [STAGES]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* pv_done = bars + 8;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 9);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* kv_full = bars + 1;                        // [STAGES]
+  uint64_t* kv_empty = kv_full + C::STAGES;            // [STAGES]
+  uint64_t* s_full = kv_empty + C::STAGES;             // [NT]
+  uint64_t* p_full = s_full + NT;                      // [NT]
+  uint64_t* pv_done = p_full + NT;                     // [NT] (last P V^T only)
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(pv_done + NT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + NT + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * (NT * BQ), h = blockIdx.y, b = blockIdx.z;
   const int nkv = int((p.nk + BKV - 1) / BKV);
 
   if (threadIdx.x == 0) {
@@ -171,10 +193,11 @@ __global__ void __launch_bounds__(THREADS, 2)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -188,19 +211,21 @@ __global__ void __launch_bounds__(THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t t_s = tmem_base, t_o = tmem_base + 128;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_expect_tx(q_full, C::Q_BYTES);
-      for (int dc = 0; dc < C::DC; ++dc)
-        tma_load_4d(sq + dc * (BQ * 128), &map_q, q_full, dc * 64, p.q_hn ? h : q0,
-                    p.q_hn ? q0 : h, b);
+      mbar_expect_tx(q_full, NT * C::Q_BYTES);
+      for (int t = 0; t < NT; ++t)
+        for (int dc = 0; dc < C::DC; ++dc) {
+          const int row = q0 + t * BQ;
+          tma_load_4d(sq + t * C::Q_BYTES + dc * (BQ * 128), &map_q, q_full, dc * 64,
+                      p.q_hn ? h : row, p.q_hn ? row : h, b);
+        }
       for (int j = 0; j < nkv && !*abort_flag; ++j) {
-        const int s = j & 1;
+        const int s = j % C::STAGES;
         if (j >= C::STAGES &&
-            !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status, ST_TIMEOUT))
+            !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, ST_TIMEOUT))
           break;
         mbar_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
         uint8_t* kt = sk + s * C::K_BYTES;
@@ -215,72 +240,77 @@ __global__ void __launch_bounds__(THREADS, 2)
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
-      // S(j + 1) is issued as soon as the softmax warps have copied S(j) to
-      // registers, so it overlaps their exponentials; O += P(j) V(j)^T
-      // follows once P(j) is written.
-      auto issue_s = [&](int j) {
-        const uint8_t* kt = sk + (j & 1) * C::K_BYTES;
+      auto issue_s = [&](int t, int j) {
+        const uint8_t* kt = sk + (j % C::STAGES) * C::K_BYTES;
+        const uint8_t* qt = sq + t * C::Q_BYTES;
 #pragma unroll
         for (int dc = 0; dc < C::DC; ++dc) {
-          const uint64_t da = smem_desc_sw128(sq + dc * (BQ * 128));
+          const uint64_t da = smem_desc_sw128(qt + dc * (BQ * 128));
           const uint64_t db = smem_desc_sw128(kt + dc * (BKV * 128));
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_f16<C::IDESC_S>(t_s, da + uint64_t(2 * k), db + uint64_t(2 * k), (dc | k) ? 1u : 0u);
+            umma_f16<C::IDESC_S>(tmem_base + C::COL_S + t * BKV, da + uint64_t(2 * k),
+                                 db + uint64_t(2 * k), (dc | k) ? 1u : 0u);
         }
-        umma_commit(s_full);
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint8_t* vt = sv + (j % C::STAGES) * C::V_BYTES;
+        const uint32_t ta = tmem_base + C::COL_S + t * BKV;  // P_t
+#pragma unroll
+        for (int kc = 0; kc < C::KA; ++kc) {
+          const uint64_t db = smem_desc_sw128(vt + kc * (D * 128));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16_ts<C::IDESC_O>(tmem_base + C::COL_O + t * D, ta + uint32_t(kc * 32 + k * 8),
+                                    db + uint64_t(2 * k), (j | kc | k) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT) &&
                 mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT);
       if (ok) {
         tc_fence_after();
-        issue_s(0);
+        for (int t = 0; t < NT; ++t) issue_s(t, 0);
       }
       for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j & 1;
-        if (j + 1 < nkv) {
-          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, ST_TIMEOUT) ||
-              !mbar_wait(s_free, j & 1, abort_flag, p.status, ST_TIMEOUT))
-            break;
+        const bool more = j + 1 < nkv;
+        for (int t = 0; t < NT && ok; ++t) {
+          // O_t += P_t(j) V(j)^T, then S_t(j+1) over the consumed P_t(j).
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
           tc_fence_after();
-          issue_s(j + 1);
+          issue_pv(t, j);
+          if (t == NT - 1) umma_commit(&kv_empty[j % C::STAGES]);
+          if (more) {
+            if (t == 0 && !mbar_wait(&kv_full[(j + 1) % C::STAGES], ((j + 1) / C::STAGES) & 1,
+                                     abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(t, j + 1);
+          } else {
+            umma_commit(&pv_done[t]);
+          }
         }
-        // O += P V^T once the softmax warps have written P (and rescaled O).
-        if (!mbar_wait(p_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) break;
-        tc_fence_after();
-        const uint8_t* vt = sv + s * C::V_BYTES;
-#pragma unroll
-        for (int kc = 0; kc < C::KA; ++kc) {
-          const uint64_t da = smem_desc_sw128(sp + kc * (BQ * 128));
-          const uint64_t db = smem_desc_sw128(vt + kc * (D * 128));
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16<C::IDESC_O>(t_o, da + uint64_t(2 * k), db + uint64_t(2 * k),
-                                 (j | kc | k) ? 1u : 0u);
-        }
-        umma_commit(&kv_empty[s]);
-        umma_commit(pv_done);
       }
     }
   } else {
     // ------------------------------------------------------ softmax / epilogue
-    const int quarter = warp & 3;
+    const int t = (warp - 2) >> 2;               // query tile of this warp
+    const int quarter = warp & 3;                // TMEM lane quarter of this warp
     const int r = quarter * 32 + lane;           // query row within the tile
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const uint32_t t_s = tmem_base + C::COL_S + t * BKV + lane_off;
+    const uint32_t t_o = tmem_base + C::COL_O + t * D + lane_off;
+    const uint32_t t_p = t_s;                    // P_t over the first half of S_t
     const float2 sc2 = f2(p.scale_log2);
     float m = -INFINITY;                         // running max, log2 units
     float2 l2 = f2(0.f);                         // running row sum (two halves)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait_idle(s_full, j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
       tc_fence_after();
       // The row's scores into registers; S is then free for S(j + 1).
       float sv[BKV];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 64) tmem_ld64(t_s + lane_off + uint32_t(c), sv + c);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
+      for (int c = 0; c < BKV; c += 64) tmem_ld64(t_s + uint32_t(c), sv + c);
       const int kvalid = int(p.nk - int64_t(j) * BKV);  // keys of this tile (may exceed BKV)
       if (kvalid < BKV) {
 #pragma unroll
@@ -297,62 +327,59 @@ __global__ void __launch_bounds__(THREADS, 2)
       const bool grow = mxs > m + RESCALE_LOG2;          // always on the first tile
       const float m_new = grow ? mxs : m;
       const float alpha = grow ? ex2f(m - m_new) : 1.f;  // 0 on the first tile
-      // The previous P V^T has finished: O is stable and the P tile is free.
+      // S_t(j) complete implies P_t(j-1) V^T complete: O_t is stable.
       if (j > 0) {
-        if (!mbar_wait_idle(pv_done, (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
-        tc_fence_after();
         if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             float o[32];
-            tmem_ld32(t_o + lane_off + uint32_t(c), o);
+            tmem_ld32(t_o + uint32_t(c), o);
+            uint32_t u[32];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
               const float2 v = mul2(make_float2(o[e], o[e + 1]), f2(alpha));
-              o[e] = v.x;
-              o[e + 1] = v.y;
+              u[e] = __float_as_uint(v.x);
+              u[e + 1] = __float_as_uint(v.y);
             }
-            tmem_st32(t_o + lane_off + uint32_t(c), o);
+            tmem_st32u(t_o + uint32_t(c), u);
           }
         }
       }
-      // P = exp2(s * scale * log2 e - m) as bf16 into the swizzled A tile
-      // (row r: BKV keys = 64-key atoms of 128 bytes), and the row sum.
+      // P = exp2(s * scale * log2 e - m) as packed bf16 pairs into the P
+      // columns of this row, and the row sum.
       const float2 nm2 = f2(-m_new);
       l2 = mul2(l2, f2(alpha));
 #pragma unroll
-      for (int c = 0; c < BKV; c += 8) {
-        float f[8];
+      for (int c = 0; c < BKV; c += 64) {
+        uint32_t u[32];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
+        for (int e = 0; e < 64; e += 2) {
           const float2 x = fma2(make_float2(sv[c + e], sv[c + e + 1]), sc2, nm2);
-          f[e] = ex2f(x.x);
-          f[e + 1] = ex2f(x.y);
-          l2 = add2(l2, make_float2(f[e], f[e + 1]));
+          const float2 f = make_float2(ex2f(x.x), ex2f(x.y));
+          l2 = add2(l2, f);
+          u[e >> 1] = pack_bf16x2(f.x, f.y);
         }
-        uint8_t* rowp = sp + (c >> 6) * (BQ * 128) + r * 128;
-        const int chunk = (c & 63) >> 3;
-        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) = pack(f, __nv_bfloat16());
+        tmem_st32u(t_p + uint32_t(c >> 1), u);
       }
+      tmem_wait_st();
       m = m_new;
-      // P is in shared memory and O is rescaled.
+      // P is in TMEM and O is rescaled.
       tc_fence_before();
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // Epilogue: O / l, bf16, after the last P V^T.
-    if (ok && nkv > 0 && mbar_wait_idle(pv_done, (nkv - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) {
+    if (ok && nkv > 0 && mbar_wait_idle(&pv_done[t], 0, abort_flag, p.status, ST_TIMEOUT)) {
       tc_fence_after();
       const float l = l2.x + l2.y;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int64_t qi = int64_t(q0) + r;
+      const int64_t qi = int64_t(q0) + t * BQ + r;
       __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + int64_t(b) * p.ob +
                             int64_t(h) * p.oh + qi * p.on;
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         float o[32];
-        tmem_ld32(t_o + lane_off + uint32_t(c), o);
+        tmem_ld32(t_o + uint32_t(c), o);
         if (qi < p.nq) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -525,7 +552,7 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
   p.oh = out->strides[1];
   p.on = out->strides[2];
   p.status = status;
-  const dim3 grid(unsigned((nq + BQ - 1) / BQ), unsigned(H), unsigned(B));
+  const dim3 grid(unsigned((nq + NT * BQ - 1) / (NT * BQ)), unsigned(H), unsigned(B));
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {

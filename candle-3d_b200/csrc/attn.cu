@@ -4,29 +4,36 @@
 //
 //   out[b, h, i, :] = softmax_j(q[b,h,i,:] . k[b,h,j,:] * scale) v[b,h,j,:]
 //
-// One CTA per (256 queries = two 128-row tiles, head, batch), 10 warps, one
-// CTA per SM:
+// One CTA per (256 queries = two 128-row tiles, head, batch), one CTA per SM:
 //   warp 0     TMA producer: both Q tiles once, then a ring of K tiles (128
 //              keys x D) and V^T tiles (D x 128 keys; V is transposed once
 //              per call into the workspace so that both products take K-major
 //              operands);
-//   warp 1     MMA issuer.  Per key tile j and query tile t: O_t += P_t(j)
-//              V(j)^T (M 128, N D, K 128, P_t read from tensor memory) as soon
-//              as the softmax warps of t have written P_t(j), then S_t(j+1) =
-//              Q_t K(j+1)^T (M 128, N 128, K D, operands in shared memory).
-//              The two query tiles share each K / V load and alternate: while
-//              one tile's softmax runs, the tensor core works for the other;
-//   warps 2-9  softmax / epilogue, warps 2-5 for tile 0 and 6-9 for tile 1,
-//              one query row per thread (its TMEM lane): the row of S_t(j) is
-//              copied to registers, the running O_t is rescaled in TMEM when
-//              the max grows past the threshold, P = exp2(S * scale * log2 e
-//              - m) is stored to TMEM as packed bf16 over the first half of
-//              S_t's columns and the row sum accumulated; after the last tile
-//              O / l is stored.
-// Each tcgen05.commit tracks every MMA issued before it, and the MMAs of one
-// thread run in issue order, so "S_t(j+1) complete" also means that P_t(j) has
-// been consumed and O_t is stable: the softmax warps wait on one barrier per
-// tile.  TMEM (512 columns): S_0 / P_0, S_1 / P_1 (128 each), O_0, O_1 (D each).
+//   MMA warps  S_t(j) = Q_t K(j)^T (M 128, N 128, K D, operands in shared
+//              memory) and O_t += P_t(j) V(j)^T (M 128, N D, K 128, P_t read
+//              from tensor memory).  The two query tiles share each K / V
+//              load; while one tile's softmax runs, the tensor core works for
+//              the other.
+//              D = 128: one MMA warp; TMEM is full, so P_t lies over the first
+//              half of S_t and per key tile the order is O_0 += P_0 V, S_0(j+1),
+//              O_1 += P_1 V, S_1(j+1).  Each tcgen05.commit tracks every MMA
+//              issued before it and one thread's MMAs run in issue order, so
+//              "S_t(j+1) complete" also means that P_t(j) has been consumed
+//              and O_t is stable: the softmax warps wait on one barrier per
+//              key tile.
+//              D = 64: one MMA warp per query tile and P_t in columns of its
+//              own, so S_t(j+1) is issued as soon as the softmax warps have
+//              copied S_t(j) to registers (it overlaps their exponentials),
+//              and O_t += P_t(j) V^T once P_t(j) is written;
+//   softmax    four warps per query tile, one query row per thread (its TMEM
+//              lane): the row of S_t(j) is copied to registers, the running
+//              O_t is rescaled in TMEM when the max grows past the threshold,
+//              P = exp2(S * scale * log2 e - m) is stored to TMEM as packed
+//              bf16 and the row sum accumulated (at D = 64 a quarter of the
+//              exponentials on the FMA pipe); after the last tile O / l is
+//              stored.
+// TMEM (512 columns): S_0, S_1 (128 each), O_0, O_1 (D each), and for D = 64
+// P_0, P_1 (64 each).
 // Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry the CTA
 // records an error in the workspace status word and stops.
 #include "common.cuh"
@@ -39,7 +46,6 @@ using namespace l3d::tc;
 
 constexpr int BQ = 128;               // rows of one query tile
 constexpr int NT = 2;                  // query tiles per CTA
-constexpr int THREADS = (2 + 4 * NT) * 32;
 constexpr int TMEM_COLS = 512;
 constexpr int ST_TIMEOUT = 5;
 constexpr int ST_MISALIGNED = 6;
@@ -47,6 +53,32 @@ constexpr int ST_MISALIGNED = 6;
 // units): until then exp2(s - m) <= 256, and O and l share the stale max, so
 // the result is unchanged while most O rescales are skipped.
 constexpr float RESCALE_LOG2 = 8.f;
+
+// exp2 on the FMA pipe, for part of the elements, so that the MUFU unit (16
+// exp2 per clock per SM) is not the only one doing them: Cody-Waite style
+// range reduction x = j + f with j = round(x) (the 1.5 * 2^23 shifter) and f
+// in [-1/2, 1/2], 2^f by a degree-3 minimax polynomial (Remez fit made for
+// this kernel, relative error 7.5e-5, far below the bf16 rounding of P), and
+// 2^j added to the exponent field.  x is clamped to -126 so that the exponent
+// stays in range; the inputs here are <= 2^8 (the rescale threshold).
+constexpr float EX2_C0 = 0.99992806f, EX2_C1 = 0.69326097f, EX2_C2 = 0.24261113f,
+                EX2_C3 = 0.05517167f;
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+  const float2 t = add2(x, f2(12582912.f));          // low mantissa bits = round(x)
+  const float2 r = add2(t, f2(-12582912.f));
+  const float2 f = add2(x, make_float2(-r.x, -r.y));
+  float2 q = fma2(f, f2(EX2_C3), f2(EX2_C2));
+  q = fma2(q, f, f2(EX2_C1));
+  q = fma2(q, f, f2(EX2_C0));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+// Of every 8 pairs of P at D = 64, this many take ex2_poly2, the rest the MUFU.
+#ifndef L3D_ATTN_POLY_PAIRS
+#define L3D_ATTN_POLY_PAIRS 2
+#endif
+constexpr int POLY_PAIRS = L3D_ATTN_POLY_PAIRS;
 
 template <int D>
 struct Cfg {
@@ -62,9 +94,22 @@ struct Cfg {
   static constexpr int SMEM = NT * Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 256;
   static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
   static constexpr uint32_t IDESC_O = make_idesc(128, D);
-  // TMEM columns (P_t over the first half of S_t)
+  // TMEM columns.  For D = 64, P_t has columns of its own (SEP_P), so that
+  // S_t(j+1) can be computed while the softmax of tile j still runs; for
+  // D = 128 TMEM is full and P_t goes over the first half of S_t.
   static constexpr uint32_t COL_S = 0, COL_O = 2 * BKV;
+  static constexpr bool SEP_P = COL_O + 2 * D + 2 * (BKV / 2) <= TMEM_COLS;
+  static constexpr uint32_t COL_P = SEP_P ? COL_O + 2 * D : COL_S;
+  static constexpr uint32_t P_STRIDE = SEP_P ? BKV / 2 : BKV;  // between P_0 and P_1
   static_assert(COL_O + 2 * D <= TMEM_COLS, "TMEM budget");
+  // MMA warps: with SEP_P one per query tile, so that the two tiles' issue
+  // chains do not wait on each other; without it one warp issues both tiles
+  // in a fixed interleave (P_0 V, S_0, P_1 V, S_1), which measured faster.
+  static constexpr int NMMA = SEP_P ? NT : 1;
+  static constexpr int THREADS = (1 + NMMA + 4 * NT) * 32;  // producer, MMA, softmax
+  // Of every 8 pairs of P, this many take ex2_poly2 (D = 64 is bound by the
+  // MUFU; at D = 128 the MUFU has room).
+  static constexpr int POLY = D == 64 ? POLY_PAIRS : 0;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -159,7 +204,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_vt, const Params p) {
   using C = Cfg<D>;
@@ -179,9 +224,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* kv_empty = kv_full + C::STAGES;            // [STAGES]
   uint64_t* s_full = kv_empty + C::STAGES;             // [NT]
   uint64_t* p_full = s_full + NT;                      // [NT]
-  uint64_t* pv_done = p_full + NT;                     // [NT] (last P V^T only)
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(pv_done + NT);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + NT + 1);
+  uint64_t* pv_done = p_full + NT;                     // [NT] (SEP_P: every P V^T; else the last)
+  uint64_t* s_free = pv_done + NT;                     // [NT] (SEP_P only)
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(s_free + NT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + NT + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * (NT * BQ), h = blockIdx.y, b = blockIdx.z;
@@ -191,11 +237,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(q_full, 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], C::NMMA);  // one commit per MMA warp
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
+      mbar_init(&s_free[t], 4);
       mbar_init(&pv_done[t], 1);
     }
     *abort_flag = 0;
@@ -237,9 +284,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_4d(vt + kc * (D * 128), &map_vt, &kv_full[s], j * BKV + kc * 64, 0, h, b);
       }
     }
-  } else if (warp == 1) {
-    // ----------------------------------------------------------------- MMA
+  } else if (warp <= C::NMMA) {
+    // ------------------------------------------------------------------ MMA
+    // Each MMA warp issues for its query tiles (t0 .. t0 + NT / NMMA); all
+    // read the same K / V stages and each commits the stage's release once
+    // its products are issued.
     if (lane == 0) {
+      constexpr int TPW = NT / C::NMMA;
+      const int t0 = (warp - 1) * TPW;
       auto issue_s = [&](int t, int j) {
         const uint8_t* kt = sk + (j % C::STAGES) * C::K_BYTES;
         const uint8_t* qt = sq + t * C::Q_BYTES;
@@ -256,7 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       auto issue_pv = [&](int t, int j) {
         const uint8_t* vt = sv + (j % C::STAGES) * C::V_BYTES;
-        const uint32_t ta = tmem_base + C::COL_S + t * BKV;  // P_t
+        const uint32_t ta = tmem_base + C::COL_P + t * C::P_STRIDE;
 #pragma unroll
         for (int kc = 0; kc < C::KA; ++kc) {
           const uint64_t db = smem_desc_sw128(vt + kc * (D * 128));
@@ -270,36 +322,60 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT);
       if (ok) {
         tc_fence_after();
-        for (int t = 0; t < NT; ++t) issue_s(t, 0);
+        for (int t = t0; t < t0 + TPW; ++t) issue_s(t, 0);
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const bool more = j + 1 < nkv;
-        for (int t = 0; t < NT && ok; ++t) {
-          // O_t += P_t(j) V(j)^T, then S_t(j+1) over the consumed P_t(j).
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (t == NT - 1) umma_commit(&kv_empty[j % C::STAGES]);
-          if (more) {
-            if (t == 0 && !mbar_wait(&kv_full[(j + 1) % C::STAGES], ((j + 1) / C::STAGES) & 1,
-                                     abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+        bool kv_ready = !more;
+        auto wait_kv = [&]() {
+          if (!kv_ready)
+            kv_ready = mbar_wait(&kv_full[(j + 1) % C::STAGES], ((j + 1) / C::STAGES) & 1,
+                                 abort_flag, p.status, ST_TIMEOUT);
+          return kv_ready;
+        };
+        for (int t = t0; ok && t < t0 + TPW; ++t) {
+          if constexpr (C::SEP_P) {
+            // S_t(j+1) as soon as the softmax warps have copied S_t(j) to
+            // registers, then O_t += P_t(j) V(j)^T once P_t(j) is written.
+            if (more) {
+              if (!wait_kv() || !mbar_wait(&s_free[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(t, j + 1);
+            }
+            if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
             tc_fence_after();
-            issue_s(t, j + 1);
-          } else {
+            issue_pv(t, j);
             umma_commit(&pv_done[t]);
+            if (t == t0 + TPW - 1) umma_commit(&kv_empty[j % C::STAGES]);
+          } else {
+            // O_t += P_t(j) V(j)^T, then S_t(j+1) over the consumed P_t(j).
+            if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j);
+            if (t == t0 + TPW - 1) umma_commit(&kv_empty[j % C::STAGES]);
+            if (more) {
+              if (!wait_kv()) { ok = false; break; }
+              tc_fence_after();
+              issue_s(t, j + 1);
+            } else {
+              umma_commit(&pv_done[t]);
+            }
           }
         }
       }
     }
   } else {
     // ------------------------------------------------------ softmax / epilogue
-    const int t = (warp - 2) >> 2;               // query tile of this warp
+    const int t = (warp - 1 - C::NMMA) >> 2;     // query tile of this warp
     const int quarter = warp & 3;                // TMEM lane quarter of this warp
     const int r = quarter * 32 + lane;           // query row within the tile
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const uint32_t t_s = tmem_base + C::COL_S + t * BKV + lane_off;
     const uint32_t t_o = tmem_base + C::COL_O + t * D + lane_off;
-    const uint32_t t_p = t_s;                    // P_t over the first half of S_t
+    const uint32_t t_p = tmem_base + C::COL_P + t * C::P_STRIDE + lane_off;
     const float2 sc2 = f2(p.scale_log2);
     float m = -INFINITY;                         // running max, log2 units
     float2 l2 = f2(0.f);                         // running row sum (two halves)
@@ -311,6 +387,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       float sv[BKV];
 #pragma unroll
       for (int c = 0; c < BKV; c += 64) tmem_ld64(t_s + uint32_t(c), sv + c);
+      if constexpr (C::SEP_P) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+      }
       const int kvalid = int(p.nk - int64_t(j) * BKV);  // keys of this tile (may exceed BKV)
       if (kvalid < BKV) {
 #pragma unroll
@@ -327,9 +408,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool grow = mxs > m + RESCALE_LOG2;          // always on the first tile
       const float m_new = grow ? mxs : m;
       const float alpha = grow ? ex2f(m - m_new) : 1.f;  // 0 on the first tile
-      // S_t(j) complete implies P_t(j-1) V^T complete: O_t is stable.
+      // Without SEP_P, S_t(j) complete implies P_t(j-1) V^T complete: O_t is
+      // stable and P_t free.  With SEP_P that is waited for here, before a
+      // rescale, or else just before P is stored.
+      bool pv_waited = !C::SEP_P || j == 0;
       if (j > 0) {
         if (__any_sync(0xffffffffu, grow)) {
+          if (!pv_waited) {
+            if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+            tc_fence_after();
+            pv_waited = true;
+          }
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             float o[32];
@@ -349,18 +438,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       // columns of this row, and the row sum.
       const float2 nm2 = f2(-m_new);
       l2 = mul2(l2, f2(alpha));
+      uint32_t u[BKV / 2];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 64) {
-        uint32_t u[32];
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          const float2 x = fma2(make_float2(sv[c + e], sv[c + e + 1]), sc2, nm2);
-          const float2 f = make_float2(ex2f(x.x), ex2f(x.y));
-          l2 = add2(l2, f);
-          u[e >> 1] = pack_bf16x2(f.x, f.y);
-        }
-        tmem_st32u(t_p + uint32_t(c >> 1), u);
+      for (int e = 0; e < BKV; e += 2) {
+        const float2 x = fma2(make_float2(sv[e], sv[e + 1]), sc2, nm2);
+        const float2 f = ((e >> 1) & 7) < C::POLY ? ex2_poly2(x)
+                                                      : make_float2(ex2f(x.x), ex2f(x.y));
+        l2 = add2(l2, f);
+        u[e >> 1] = pack_bf16x2(f.x, f.y);
       }
+      if (!pv_waited) {  // P_t(j-1) V^T has read P_t
+        if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int c = 0; c < BKV / 2; c += 32) tmem_st32u(t_p + uint32_t(c), u + c);
       tmem_wait_st();
       m = m_new;
       // P is in TMEM and O is rescaled.
@@ -369,7 +461,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // Epilogue: O / l, bf16, after the last P V^T.
-    if (ok && nkv > 0 && mbar_wait_idle(&pv_done[t], 0, abort_flag, p.status, ST_TIMEOUT)) {
+    if (ok && nkv > 0 &&
+        mbar_wait_idle(&pv_done[t], C::SEP_P ? (nkv - 1) & 1 : 0, abort_flag, p.status, ST_TIMEOUT)) {
       tc_fence_after();
       const float l = l2.x + l2.y;
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -563,7 +656,7 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
                                   Cfg<128>::SMEM);
   });
   if (attr != cudaSuccess) return fail(L3D_E_CUDA, "%s: cannot reserve shared memory", op);
-  if (D == 64) attn_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, s>>>(map_q, map_k, map_vt, p);
-  else attn_kernel<128><<<grid, THREADS, Cfg<128>::SMEM, s>>>(map_q, map_k, map_vt, p);
+  if (D == 64) attn_kernel<64><<<grid, Cfg<64>::THREADS, Cfg<64>::SMEM, s>>>(map_q, map_k, map_vt, p);
+  else attn_kernel<128><<<grid, Cfg<128>::THREADS, Cfg<128>::SMEM, s>>>(map_q, map_k, map_vt, p);
   return check_launch(op);
 }

@@ -5,13 +5,12 @@
 //   out[b, h, i, :] = softmax_j(q[b,h,i,:] . k[b,h,j,:] * scale) v[b,h,j,:]
 //
 // One CTA per (256 queries = two 128-row tiles, head, batch), one CTA per SM:
-//   warp 0     TMA producer: both Q tiles once, then a ring of K tiles (128
-//              keys x D) and V^T tiles (D x 128 keys; V is transposed once
-//              per call into the workspace so that both products take K-major
-//              operands);
+//   warp 0     TMA producer: both Q tiles once, then a ring of K and V tiles
+//              (128 keys x D each, 128B-swizzled boxes of 64 columns), read
+//              in place from the caller's (possibly strided) views;
 //   MMA warps  S_t(j) = Q_t K(j)^T (M 128, N 128, K D, operands in shared
-//              memory) and O_t += P_t(j) V(j)^T (M 128, N D, K 128, P_t read
-//              from tensor memory).  The two query tiles share each K / V
+//              memory) and O_t += P_t(j) V(j) (M 128, N D, K 128, P_t read
+//              from tensor memory, V as an MN-major operand: D contiguous).  The two query tiles share each K / V
 //              load; while one tile's softmax runs, the tensor core works for
 //              the other.
 //              D = 128: one MMA warp; TMEM is full, so P_t lies over the first
@@ -84,16 +83,15 @@ template <int D>
 struct Cfg {
   static constexpr int BKV = 128;
   static constexpr int DC = D / 64;                   // 64-wide K atoms of Q / K
-  static constexpr int KA = BKV / 64;                 // 64-key atoms of V^T
   static constexpr int Q_BYTES = BQ * D * 2;          // one query tile
   static constexpr int K_BYTES = BKV * D * 2;
-  static constexpr int V_BYTES = D * BKV * 2;         // V^T tile: D rows x BKV keys
+  static constexpr int V_BYTES = BKV * D * 2;         // V tile: BKV keys x D
   static constexpr int STAGES = D == 64 ? 4 : 2;
   // No alignment slack: with no static shared memory the dynamic window
   // starts 1024-byte aligned (checked at run time).
   static constexpr int SMEM = NT * Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 256;
   static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
-  static constexpr uint32_t IDESC_O = make_idesc(128, D);
+  static constexpr uint32_t IDESC_O = make_idesc(128, D) | (1u << 16);  // B (V) MN-major
   // TMEM columns.  For D = 64, P_t has columns of its own (SEP_P), so that
   // S_t(j+1) can be computed while the softmax of tile j still runs; for
   // D = 128 TMEM is full and P_t goes over the first half of S_t.
@@ -115,7 +113,7 @@ struct Cfg {
 
 struct Params {
   int64_t nq, nk;       // query / key lengths
-  int q_hn, k_hn;       // the q / k maps list heads before rows (token-major memory)
+  int q_hn, k_hn, v_hn; // the q / k / v maps list heads before rows (token-major memory)
   float scale_log2;     // softmax scale * log2(e), > 0
   void* out;            // [B, H, nq, D] bf16
   int64_t ob, oh, on;   // out strides (elements)
@@ -130,6 +128,20 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+
+// MN-major, 128B-swizzled operand tile (B = V: N = D contiguous in rows of 128
+// B, one row per K index): 8-row K groups 1024 B apart (SBO), 64-wide N blocks
+// `lbo` bytes apart (LBO).
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(const void* tile, uint32_t lbo) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3fffull;
+  d |= uint64_t((lbo >> 4) & 0x3fff) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]^T: A (M 128 x K 16, bf16 pairs packed in 32-bit
@@ -206,7 +218,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 template <int D>
 __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                const __grid_constant__ CUtensorMap map_vt, const Params p) {
+                const __grid_constant__ CUtensorMap map_v, const Params p) {
   using C = Cfg<D>;
   constexpr int BKV = C::BKV;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -217,7 +229,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   }
   uint8_t* sq = smem_raw;                              // [NT][DC][128 x 64]
   uint8_t* sk = sq + NT * C::Q_BYTES;                  // [STAGES][DC][BKV x 64]
-  uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][KA][D x 64]
+  uint8_t* sv = sk + C::STAGES * C::K_BYTES;           // [STAGES][DC][BKV x 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sv + C::STAGES * C::V_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                        // [STAGES]
@@ -280,8 +292,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           tma_load_4d(kt + dc * (BKV * 128), &map_k, &kv_full[s], dc * 64, p.k_hn ? h : j * BKV,
                       p.k_hn ? j * BKV : h, b);
         uint8_t* vt = sv + s * C::V_BYTES;
-        for (int kc = 0; kc < C::KA; ++kc)
-          tma_load_4d(vt + kc * (D * 128), &map_vt, &kv_full[s], j * BKV + kc * 64, 0, h, b);
+        for (int dc = 0; dc < C::DC; ++dc)
+          tma_load_4d(vt + dc * (BKV * 128), &map_v, &kv_full[s], dc * 64, p.v_hn ? h : j * BKV,
+                      p.v_hn ? j * BKV : h, b);
       }
     }
   } else if (warp <= C::NMMA) {
@@ -309,14 +322,12 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       auto issue_pv = [&](int t, int j) {
         const uint8_t* vt = sv + (j % C::STAGES) * C::V_BYTES;
         const uint32_t ta = tmem_base + C::COL_P + t * C::P_STRIDE;
+        // K step of 16 keys = 16 rows of 128 B; P advances 8 columns.
+        const uint64_t db = smem_desc_sw128_mn(vt, BKV * 128);
 #pragma unroll
-        for (int kc = 0; kc < C::KA; ++kc) {
-          const uint64_t db = smem_desc_sw128(vt + kc * (D * 128));
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16_ts<C::IDESC_O>(tmem_base + C::COL_O + t * D, ta + uint32_t(kc * 32 + k * 8),
-                                    db + uint64_t(2 * k), (j | kc | k) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < BKV / 16; ++ks)
+          umma_f16_ts<C::IDESC_O>(tmem_base + C::COL_O + t * D, ta + uint32_t(ks * 8),
+                                  db + uint64_t(ks * (16 * 128 >> 4)), (j | ks) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT) &&
                 mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT);
@@ -502,30 +513,6 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   }
 }
 
-// v [B, H, nk, D] -> vt [B, H, D, ldk] (keys contiguous, zero past nk).
-__global__ void transpose_v_kernel(const __nv_bfloat16* __restrict__ v, int64_t sb, int64_t sh,
-                                   int64_t sn, int H, int64_t nk, int D, int64_t ldk,
-                                   __nv_bfloat16* __restrict__ vt) {
-  __shared__ __nv_bfloat16 tile[32][33];
-  const int bh = blockIdx.z;
-  const int b = bh / H, h = bh - b * H;
-  const int64_t k0 = int64_t(blockIdx.x) * 32;
-  const int d0 = blockIdx.y * 32;
-  const __nv_bfloat16* vb = v + int64_t(b) * sb + int64_t(h) * sh;
-  __nv_bfloat16* ob = vt + int64_t(bh) * D * ldk;
-  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
-    const int64_t key = k0 + y;
-    const int d = d0 + threadIdx.x;
-    tile[y][threadIdx.x] = (key < nk && d < D) ? vb[key * sn + d] : __float2bfloat16(0.f);
-  }
-  __syncthreads();
-  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
-    const int d = d0 + y;
-    const int64_t key = k0 + threadIdx.x;
-    if (d < D && key < ldk) ob[int64_t(d) * ldk + key] = tile[threadIdx.x][y];
-  }
-}
-
 // 4-D bf16 view [B, H, rows, cols] (cols contiguous) as a TMA map with a box
 // of 64 columns x box_rows rows, 128B swizzle.  The map's dimensions are
 // ordered by stride: (cols, rows, H, B), or (cols, H, rows, B) when heads are
@@ -551,8 +538,6 @@ static bool make_map4(CUtensorMap* m, const void* base, int64_t B, int64_t H, in
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-
 }  // namespace attn
 }  // namespace l3d
 
@@ -560,8 +545,7 @@ using namespace l3d;
 
 extern "C" size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk, int64_t d) {
   if (b < 0 || h < 0 || nk < 0 || d < 0) return 0;
-  const int64_t ldk = (nk + 7) / 8 * 8;
-  return 256 + attn::align256(size_t(b) * size_t(h) * size_t(d) * size_t(ldk) * 2);
+  return 256;  // the status word; q, k and v are read in place
 }
 
 extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v,
@@ -617,26 +601,19 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
     }
     return fail(L3D_E_UNSUPPORTED, "%s: empty keys need a contiguous out", op);
   }
-  // V^T [B, H, D, ldk] in the workspace.
-  const int64_t ldk = (nk + 7) / 8 * 8;
-  __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(ws + 256);
-  {
-    const dim3 grid(unsigned((ldk + 31) / 32), unsigned((D + 31) / 32), unsigned(B * H));
-    transpose_v_kernel<<<grid, dim3(32, 8), 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16*>(elem_ptr(v)), v->strides[0], v->strides[1],
-        v->strides[2], int(H), nk, int(D), ldk, vt);
-  }
-  CUtensorMap map_q, map_k, map_vt;
+  CUtensorMap map_q, map_k, map_v;
   int q_hn = 0, k_hn = 0, v_hn = 0;
   if (!make_map4(&map_q, elem_ptr(q), B, H, nq, D, q->strides[2], q->strides[1], q->strides[0], BQ,
                  &q_hn) ||
       !make_map4(&map_k, elem_ptr(k), B, H, nk, D, k->strides[2], k->strides[1], k->strides[0],
                  uint32_t(D == 64 ? Cfg<64>::BKV : Cfg<128>::BKV), &k_hn) ||
-      !make_map4(&map_vt, vt, B, H, D, ldk, ldk, D * ldk, H * D * ldk, uint32_t(D), &v_hn) || v_hn)
+      !make_map4(&map_v, elem_ptr(v), B, H, nk, D, v->strides[2], v->strides[1], v->strides[0],
+                 uint32_t(Cfg<64>::BKV), &v_hn))
     return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed", op);
   Params p{};
   p.q_hn = q_hn;
   p.k_hn = k_hn;
+  p.v_hn = v_hn;
   p.nq = nq;
   p.nk = nk;
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -656,7 +633,7 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
                                   Cfg<128>::SMEM);
   });
   if (attr != cudaSuccess) return fail(L3D_E_CUDA, "%s: cannot reserve shared memory", op);
-  if (D == 64) attn_kernel<64><<<grid, Cfg<64>::THREADS, Cfg<64>::SMEM, s>>>(map_q, map_k, map_vt, p);
-  else attn_kernel<128><<<grid, Cfg<128>::THREADS, Cfg<128>::SMEM, s>>>(map_q, map_k, map_vt, p);
+  if (D == 64) attn_kernel<64><<<grid, Cfg<64>::THREADS, Cfg<64>::SMEM, s>>>(map_q, map_k, map_v, p);
+  else attn_kernel<128><<<grid, Cfg<128>::THREADS, Cfg<128>::SMEM, s>>>(map_q, map_k, map_v, p);
   return check_launch(op);
 }

@@ -354,7 +354,7 @@ int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor* pair_src,
 
 /* ---- next row: the attention core --------------------------------------------- */
 
-/* Workspace bytes for l3d_attention. */
+/* Workspace bytes for l3d_attention (256: the status word). */
 size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk, int64_t d);
 
 /* exact_sdpa_heads / exact_query_chunked_sdpa
@@ -363,8 +363,9 @@ size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk, int64_t d)
  * softmax in f32, P rounded to bf16 for the second product).  q [B, H, N, D],
  * k and v [B, H, Nk, D], out [B, H, N, D], BF16, D = 64 or 128, any strides
  * with the head dim contiguous and 16-byte multiples elsewhere (e.g. views of
- * a [B, N, 3, H, D] projection or token-major [B, N, H, D] memory).  The
- * workspace holds V transposed and a status word. */
+ * a [B, N, 3, H, D] projection or token-major [B, N, H, D] memory), read in
+ * place.  scale must be positive.  The workspace holds a status word (0 = ok;
+ * non-zero = a bounded wait inside the kernel expired). */
 int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v, float scale,
                   const l3d_tensor* out, void* workspace, size_t workspace_bytes,
                   l3d_stream stream);

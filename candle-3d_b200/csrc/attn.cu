@@ -244,12 +244,17 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * (NT * BQ), h = blockIdx.y, b = blockIdx.z;
   const int nkv = int((p.nk + BKV - 1) / BKV);
+  // Query tiles of this CTA that hold rows (the second one can lie wholly
+  // past nq in the last block); empty tiles are skipped by every role.
+  const int ntv = int((p.nq - q0 + BQ - 1) / BQ) < NT ? int((p.nq - q0 + BQ - 1) / BQ) : NT;
+  // MMA warps with work: each commits the release of every K / V stage.
+  const int nmma = C::SEP_P ? ntv : 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], C::NMMA);  // one commit per MMA warp
+      mbar_init(&kv_empty[s], nmma);  // one commit per MMA warp with work
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&s_full[t], 1);
@@ -274,8 +279,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_expect_tx(q_full, NT * C::Q_BYTES);
-      for (int t = 0; t < NT; ++t)
+      mbar_expect_tx(q_full, ntv * C::Q_BYTES);
+      for (int t = 0; t < ntv; ++t)
         for (int dc = 0; dc < C::DC; ++dc) {
           const int row = q0 + t * BQ;
           tma_load_4d(sq + t * C::Q_BYTES + dc * (BQ * 128), &map_q, q_full, dc * 64,
@@ -302,9 +307,10 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     // Each MMA warp issues for its query tiles (t0 .. t0 + NT / NMMA); all
     // read the same K / V stages and each commits the stage's release once
     // its products are issued.
-    if (lane == 0) {
-      constexpr int TPW = NT / C::NMMA;
-      const int t0 = (warp - 1) * TPW;
+    constexpr int TPW = NT / C::NMMA;
+    const int t0 = (warp - 1) * TPW;
+    const int t1 = min(t0 + TPW, ntv);  // this warp's tiles with rows: t0 .. t1 - 1
+    if (lane == 0 && t0 < t1) {
       auto issue_s = [&](int t, int j) {
         const uint8_t* kt = sk + (j % C::STAGES) * C::K_BYTES;
         const uint8_t* qt = sq + t * C::Q_BYTES;
@@ -333,7 +339,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                 mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT);
       if (ok) {
         tc_fence_after();
-        for (int t = t0; t < t0 + TPW; ++t) issue_s(t, 0);
+        for (int t = t0; t < t1; ++t) issue_s(t, 0);
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const bool more = j + 1 < nkv;
@@ -344,7 +350,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
                                  abort_flag, p.status, ST_TIMEOUT);
           return kv_ready;
         };
-        for (int t = t0; ok && t < t0 + TPW; ++t) {
+        for (int t = t0; ok && t < t1; ++t) {
           if constexpr (C::SEP_P) {
             // S_t(j+1) as soon as the softmax warps have copied S_t(j) to
             // registers, then O_t += P_t(j) V(j)^T once P_t(j) is written.
@@ -360,13 +366,13 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             tc_fence_after();
             issue_pv(t, j);
             umma_commit(&pv_done[t]);
-            if (t == t0 + TPW - 1) umma_commit(&kv_empty[j % C::STAGES]);
+            if (t == t1 - 1) umma_commit(&kv_empty[j % C::STAGES]);
           } else {
             // O_t += P_t(j) V(j)^T, then S_t(j+1) over the consumed P_t(j).
             if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, j);
-            if (t == t0 + TPW - 1) umma_commit(&kv_empty[j % C::STAGES]);
+            if (t == t1 - 1) umma_commit(&kv_empty[j % C::STAGES]);
             if (more) {
               if (!wait_kv()) { ok = false; break; }
               tc_fence_after();
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         }
       }
     }
-  } else {
+  } else if ((warp - 1 - C::NMMA) >> 2 < ntv) {
     // ------------------------------------------------------ softmax / epilogue
     const int t = (warp - 1 - C::NMMA) >> 2;     // query tile of this warp
     const int quarter = warp & 3;                // TMEM lane quarter of this warp

@@ -102,3 +102,48 @@ def test_attention_rejects_bad_scale(ops, dev):
     q = torch.zeros(1, 1, 8, 64, device=dev, dtype=torch.bfloat16)
     with pytest.raises(Exception, match="scale"):
         ops.attention(q, q, q, -1.0)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_single_key_returns_v(ops, dev, D):
+    """softmax over one key is 1: every output row is that key's v row."""
+    import torch
+
+    g = torch.Generator().manual_seed(D)
+    q = torch.randn(2, 3, 300, D, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(2, 3, 1, D, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(2, 3, 1, D, generator=g).to(dev, torch.bfloat16)
+    out = ops.attention(q, k, v, D ** -0.5)
+    torch.cuda.synchronize()
+    assert torch.equal(out, v.expand(2, 3, 300, D))
+
+
+def test_attention_empty_keys_give_zeros(ops, dev):
+    import torch
+
+    q = torch.randn(1, 2, 40, 64, device=dev).to(torch.bfloat16)
+    kv = torch.zeros(1, 2, 0, 64, device=dev, dtype=torch.bfloat16)
+    out = ops.attention(q, kv, kv, 0.125, out=torch.full_like(q, 7.0))
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_one_query_odd_heads_strided_out(ops, dev, D):
+    """nq = 1 (one row in a 256-row block), B x H = 3 x 5, and an output that
+    is a view into a wider buffer."""
+    import torch
+
+    g = torch.Generator().manual_seed(7 + D)
+    B, H, NK = 3, 5, 517
+    q = torch.randn(B, H, 1, D, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(B, H, NK, D, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(B, H, NK, D, generator=g).to(dev, torch.bfloat16)
+    buf = torch.zeros(B, 1, H, 2 * D, device=dev, dtype=torch.bfloat16)
+    out = buf[..., :D].transpose(1, 2)  # [B, H, 1, D] with strides (H*2D, 2D, H*2D, 1)
+    ops.attention(q, k, v, D ** -0.5, out=out)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(buf[..., D:]).item() == 0  # nothing written past the view
+    ref = _ref(q, k, v, D ** -0.5)
+    err = (out.float() - ref).abs()
+    assert torch.all(err <= 2e-2 * torch.clamp(ref.abs(), min=1.0)), f"max err {err.max().item():.3e}"

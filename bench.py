@@ -59,6 +59,9 @@ def parse():
                          "Q8_0 linears of one config-4 block (TFLOP/s); sparseconv: the "
                          "TRELLIS.2 VAE's first submanifold conv (TFLOP/s); attention: "
                          "the attention core of one block (TFLOP/s, --attn-case)")
+    ap.add_argument("--attention", default="sdpa", choices=["sdpa", "l3d"],
+                    help="vggt / triposg / trellis: the stacks' bf16 attention core (torch SDPA "
+                         "or l3d_attention)")
     ap.add_argument("--attn-case", default="vggt-global", choices=list(ATTN_CASES),
                     help="attention workload: which block's attention (B, H, N, D)")
     ap.add_argument("--conv-channels", type=int, default=1024,
@@ -297,6 +300,7 @@ def run_vggt(args, world, rank, local):
     pkg = graft.load_package()
     from candle3d_b200 import blocks
 
+    blocks.set_attention(args.attention)
     ops = pkg.ops
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -359,7 +363,7 @@ def run_vggt(args, world, rank, local):
         "config": {"workload": "config2 VGGT-1B aggregator: patch embed + 24 frame / 24 global "
                                "blocks, S=8 views x 1374 tokens, dim 1024, 16 heads, MLP 4096",
                    "parallelism": "single GPU (global attention couples all views)",
-                   "baseline_metric": BASELINE_METRIC},
+                   "attention": args.attention, "baseline_metric": BASELINE_METRIC},
         "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + SDPA + fused ops)",
                      "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": round(ach / peak_tf, 4), "traffic": None},
@@ -531,6 +535,7 @@ def run_qlinear(args, local):
     graft.load_package()
     from candle3d_b200 import blocks
 
+    blocks.set_attention(args.attention)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     g = torch.Generator().manual_seed(20261201)
@@ -595,6 +600,7 @@ def run_dit(args, local):
     graft.load_package()
     from candle3d_b200 import blocks
 
+    blocks.set_attention(args.attention)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     g = torch.Generator().manual_seed(20261201)
@@ -653,7 +659,8 @@ def run_dit(args, local):
         "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": desc, "parallelism": "single GPU", "baseline_metric": BASELINE_METRIC},
+        "config": {"workload": desc, "parallelism": "single GPU", "attention": args.attention,
+                   "baseline_metric": BASELINE_METRIC},
         "clocks": clocks,
         "e2e": {"value": round(tokens * n2 / (ems / 1e3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(hp.numel() * hp.element_size()),

@@ -2,9 +2,10 @@
 
 Each stack follows the reference block's op order exactly; between the GEMMs
 (cuBLAS through torch, or the tcgen05 dequant-linear for GGML weights) and the
-attention (torch SDPA, a library kernel) every per-token op runs as one of this
-package's fused kernels, and every residual add is fused with the norm that
-follows it:
+attention (torch SDPA by default; `set_attention("l3d")` routes the bf16
+attention cores to this package's tcgen05 kernel, `ops.attention`) every
+per-token op runs as one of this package's fused kernels, and every residual
+add is fused with the norm that follows it:
 
   * VGGT aggregator (crate/runtime/vggt.rs:113-186,264-313): frame / global
     alternating blocks; LN -> qkv -> per-head LN + 2D RoPE (q and k, one launch)
@@ -30,6 +31,25 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
+
+_ATTENTION = "sdpa"
+
+
+def set_attention(impl: str) -> None:
+    """Selects the attention core of the stacks' bf16 attention: "sdpa" (torch
+    scaled_dot_product_attention, cuDNN) or "l3d" (l3d_attention)."""
+    global _ATTENTION
+    if impl not in ("sdpa", "l3d"):
+        raise ValueError(f"unknown attention implementation {impl!r}")
+    _ATTENTION = impl
+
+
+def _attend(q, k, v):
+    """exact_sdpa_heads (crate/runtime/attention_math.rs:199-259) on [B, H, N, D]
+    views, by the implementation set_attention selected."""
+    if _ATTENTION == "l3d":
+        return ops.attention(q, k, v)
+    return F.scaled_dot_product_attention(q, k, v)
 
 
 def _w(g, shape, std=0.02, dev=None, dtype=torch.bfloat16):
@@ -82,7 +102,7 @@ class VggtAggregator:
         qk = torch.empty(2, B, N, H, D, dtype=y.dtype, device=y.device).permute(0, 1, 3, 2, 4)
         q, k = ops.qk_layernorm_rope2d(qkv[0], qkv[1], p["qnw"], p["qnb"], p["knw"], p["knb"],
                                        1e-5, pos, 100.0, q_out=qk[0], k_out=qk[1])
-        a = F.scaled_dot_product_attention(q, k, qkv[2])
+        a = _attend(q, k, qkv[2])
         return F.linear(a.transpose(1, 2).reshape(B, N, C), p["proj_w"], p["proj_b"])
 
     def forward(self, tokens, frame_pos, global_pos, S):
@@ -198,7 +218,7 @@ class TripoSgDit:
         q = ops.rms_norm_heads(qkv[..., :D].transpose(1, 2), p["nq1"], 1e-6)
         k = ops.rms_norm_heads(qkv[..., D:2 * D].transpose(1, 2), p["nk1"], 1e-6)
         v = qkv[..., 2 * D:].transpose(1, 2)
-        a = F.scaled_dot_product_attention(q, k, v)
+        a = _attend(q, k, v)
         return F.linear(a.transpose(1, 2).reshape(B, L, C), p["o1_w"], p["o1_b"])
 
     def _cross_attn(self, p, y, cond):
@@ -398,16 +418,14 @@ class Trellis2Slat:
             qkv = p["to_qkv"](y).view(1, N, 3, H, D)
             q = ops.qk_l2norm_rope3d(qkv[:, :, 0], p["qg"], coords)
             k = ops.qk_l2norm_rope3d(qkv[:, :, 1], p["kg"], coords)
-            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
-                                               qkv[:, :, 2].transpose(1, 2))
+            a = _attend(q.transpose(1, 2), k.transpose(1, 2), qkv[:, :, 2].transpose(1, 2))
             o = p["to_out"](a.transpose(1, 2).reshape(1, N, C))
             x, y = ops.residual_layer_norm_modulate(x, o, gate=g_msa, weight=p["n2w"], bias=p["n2b"],
                                                     eps=1e-6, inplace=True)
             cq = ops.qk_l2norm_rope3d(p["c_q"](y).view(1, N, H, D), p["cqg"], None)
             kv = p["c_kv"](cond).view(1, Lc, 2, H, D)
             ck = ops.qk_l2norm_rope3d(kv[:, :, 0], p["ckg"], None)
-            ca = F.scaled_dot_product_attention(cq.transpose(1, 2), ck.transpose(1, 2),
-                                                kv[:, :, 1].transpose(1, 2))
+            ca = _attend(cq.transpose(1, 2), ck.transpose(1, 2), kv[:, :, 1].transpose(1, 2))
             co = p["c_out"](ca.transpose(1, 2).reshape(1, N, C))
             x, y = ops.residual_layer_norm_modulate(x, co, shift=sh_mlp, scale=sc_mlp, eps=1e-6,
                                                     inplace=True)

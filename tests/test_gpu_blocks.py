@@ -1,5 +1,6 @@
-"""GPU parity of the block stacks (fused ops + cuBLAS GEMMs + SDPA) against
-plain torch f32 restatements of the reference blocks at reduced depth/size.
+"""GPU parity of the block stacks (fused ops + cuBLAS GEMMs + attention, both
+torch SDPA and l3d_attention) against plain torch f32 restatements of the
+reference blocks at reduced depth/size.
 
 Stacks compound bf16 rounding across blocks, so the comparison is normwise:
 relative L2 error of the stack output (and of the residual-stream update)
@@ -16,7 +17,17 @@ def rel_l2(a, b):
     return float((a - b).norm() / b.norm())
 
 
-def test_vggt_stack_matches_reference(pkg, dev):
+@pytest.fixture(params=["sdpa", "l3d"])
+def attn(request, pkg):
+    """The stacks' bf16 attention core: torch SDPA, or l3d_attention."""
+    from candle3d_b200 import blocks
+
+    blocks.set_attention(request.param)
+    yield request.param
+    blocks.set_attention("sdpa")
+
+
+def test_vggt_stack_matches_reference(pkg, dev, attn):
     import torch
 
     from candle3d_b200 import blocks
@@ -37,7 +48,7 @@ def test_vggt_stack_matches_reference(pkg, dev):
     assert rel_l2(out, ref) < 2e-2
 
 
-def test_triposg_stack_matches_reference(pkg, dev):
+def test_triposg_stack_matches_reference(pkg, dev, attn):
     import torch
 
     from candle3d_b200 import blocks
@@ -54,7 +65,7 @@ def test_triposg_stack_matches_reference(pkg, dev):
     assert rel_l2(out, ref) < 2e-2
 
 
-def test_trellis_slat_stack_matches_reference(pkg, ops, dev):
+def test_trellis_slat_stack_matches_reference(pkg, ops, dev, attn):
     import torch
     import torch.nn.functional as F
 

@@ -727,8 +727,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Gather modes keep up to kGatherDepth stages of cp.async copies in
     // flight; a stage is signalled to the MMA once its copies have landed
     // (cp.async.wait_group) and a proxy fence has made them visible to the
-    // tensor core.  kGatherDepth < STAGES, so the producer can always refill
-    // the stages the gatherers wait on.
+    // tensor core.  The oldest stage is signalled as soon as kGatherDepth are
+    // pending, before the gatherers wait for the next stage to be released,
+    // so the MMA can always release the stage they wait on.
     constexpr int kGatherDepth = 3;
     int pend = 0, arr_stage = 0;
     auto retire_oldest = [&](bool all) {
@@ -748,9 +749,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       int32_t src[4];
       bool ok = true;
       for (int kb = 0; kb < kblocks; ++kb) {
-        // The stage's TMA loads have landed, which also means the MMA has
-        // released the stage's buffers.
-        if (!mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW)) {
+        // Gatherers write only the A tile: they start once the MMA has
+        // released the stage, in parallel with the weight TMA of the same
+        // stage (the MMA waits for both).  Dequantisers read the stage's raw
+        // TMA load, so they wait for it to land (which also means the MMA has
+        // released the stage's buffers).
+        const bool ready =
+            GATHER ? mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)
+                   : mbar_wait(&lfull[stage], phase, abort_flag, p.status, ST_TIMEOUT_RAW);
+        if (!ready) {
           ok = false;
           break;
         }

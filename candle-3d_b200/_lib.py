@@ -101,6 +101,8 @@ _SIGS = {
                             C.c_size_t, _S], C.c_int),
     "l3d_dequant_linear_ex": ([_P, C.c_void_p, C.c_int, C.c_int64, C.c_int64, _P, C.c_int, _P, _P,
                                _P, C.c_void_p, C.c_size_t, _S], C.c_int),
+    "l3d_linear_workspace_size": ([C.c_int64, C.c_int64, C.c_int64], C.c_size_t),
+    "l3d_linear_ex": ([_P, _P, _P, C.c_int, _P, _P, _P, C.c_void_p, C.c_size_t, _S], C.c_int),
     "l3d_sparse_neighbor_pairs_workspace_size": ([C.c_int64], C.c_size_t),
     "l3d_sparse_neighbor_pairs": ([_P, _P, _P, _P, C.c_void_p, C.c_size_t, _S], C.c_int),
     "l3d_sparse_neighbor_pairs_noalloc": ([_P, _P, _P, _P, _S], C.c_int),

@@ -905,6 +905,11 @@ constexpr int64_t kDecodeOnceRows = 512;
 // [n, k].
 static bool decode_once(int fmt, int64_t m) { return m > kDecodeOnceRows || is_kquant(fmt); }
 
+extern "C" size_t l3d_linear_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || k < 0 || n < 0) return 0;
+  return 256 + align256(size_t(m) * size_t(k) * 2);  // status word + activation copy
+}
+
 extern "C" size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t n, int64_t k) {
   if (m < 0 || k < 0 || n < 0) return 0;
   size_t bytes = 256 + align256(size_t(m) * size_t(k) * 2);
@@ -912,20 +917,37 @@ extern "C" size_t l3d_dequant_linear_workspace_size(int fmt, int64_t m, int64_t 
   return bytes;
 }
 
+// wdense: a bf16 [n, k] weight used as is (l3d_linear_ex; wq and fmt unused),
+// or NULL for GGML blocks at wq in format fmt.
 static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int64_t n, int64_t k,
                               const l3d_tensor* bias, int act, const l3d_tensor* residual,
                               const l3d_tensor* gate, const l3d_tensor* y, void* workspace,
-                              size_t workspace_bytes, l3d_stream stream, const char* op) {
+                              size_t workspace_bytes, l3d_stream stream, const char* op,
+                              const l3d_tensor* wdense = nullptr) {
   using namespace l3d::gemm;
+  int64_t w_ld = 0;
+  if (wdense) {
+    if (no_data(wdense)) return fail(L3D_E_NULL, "%s: weight has no data", op);
+    if (wdense->dtype != L3D_BF16) return fail(L3D_E_DTYPE, "%s: weight must be BF16", op);
+    if (wdense->ndim != 2) return fail(L3D_E_SHAPE, "%s: weight must be [n, k]", op);
+    n = wdense->dims[0];
+    k = wdense->dims[1];
+    w_ld = n > 1 ? wdense->strides[0] : k;
+    if (k > 1 && wdense->strides[1] != 1) return fail(L3D_E_ALIGN, "%s: weight rows must be contiguous", op);
+    wq = elem_ptr(wdense);
+    if (k % 8 || (w_ld * 2) % 16 || reinterpret_cast<uintptr_t>(wq) % 16)
+      return fail(L3D_E_ALIGN, "%s: k must be a multiple of 8 and weight rows 16-byte aligned", op);
+  }
   if (!x || !y || !wq || no_data(x) || no_data(y))
     return fail(L3D_E_NULL, "%s: x, wq and y are required", op);
-  if (!qfmt_known(fmt)) return fail(L3D_E_UNSUPPORTED, "%s: unknown format", op);
+  if (!wdense && !qfmt_known(fmt)) return fail(L3D_E_UNSUPPORTED, "%s: unknown format", op);
   if (x->dtype != L3D_BF16 && x->dtype != L3D_F32)
     return fail(L3D_E_DTYPE, "%s: x must be BF16 or F32", op);
   if (y->dtype != L3D_BF16 && y->dtype != L3D_F32)
     return fail(L3D_E_DTYPE, "%s: y must be BF16 or F32", op);
-  if (k <= 0 || k % block_elems(fmt) || n <= 0)
+  if (!wdense && (k <= 0 || k % block_elems(fmt) || n <= 0))
     return fail(L3D_E_SHAPE, "%s: k must be a positive multiple of %d", op, block_elems(fmt));
+  if (wdense && (k <= 0 || n <= 0)) return fail(L3D_E_SHAPE, "%s: empty weight", op);
   if (x->ndim < 1 || x->dims[x->ndim - 1] != k) return fail(L3D_E_SHAPE, "%s: x last dim != k", op);
   if (y->ndim != x->ndim || y->dims[y->ndim - 1] != n) return fail(L3D_E_SHAPE, "%s: y last dim != n", op);
   int64_t M = 1;
@@ -978,7 +1000,8 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
     if (numel(gate) != n || (gate->ndim >= 1 && n > 1 && gate->strides[gate->ndim - 1] != 1))
       return fail(L3D_E_SHAPE, "%s: gate must be contiguous [n]", op);
   }
-  const size_t need = l3d_dequant_linear_workspace_size(fmt, M, n, k);
+  const size_t need = wdense ? l3d_linear_workspace_size(M, n, k)
+                             : l3d_dequant_linear_workspace_size(fmt, M, n, k);
   if (!workspace || workspace_bytes < need)
     return fail(L3D_E_WORKSPACE, "%s: workspace of %zu bytes required", op, need);
   if (reinterpret_cast<uintptr_t>(workspace) % 256)
@@ -1020,8 +1043,8 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
   p.status = status;
   p.wq = static_cast<const uint8_t*>(wq);
   p.fmt = fmt;
-  p.row_bytes = (k / block_elems(fmt)) * block_bytes(fmt);
-  p.bpt = 2 * block_bytes(fmt);
+  p.row_bytes = wdense ? 0 : (k / block_elems(fmt)) * block_bytes(fmt);
+  p.bpt = wdense ? 0 : 2 * block_bytes(fmt);
   p.act = act;
   p.res = res_ptr;
   p.res_ld = res_ld;
@@ -1040,7 +1063,12 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
                     : 0;
   if (!p.tma_store) map_y = map_x;  // unused
   int mode;
-  if (decode_once(fmt, M)) {
+  if (wdense) {
+    // Dense bf16 weights: streamed by TMA as they are.
+    if (!make_map_x(&map_w, wq, uint64_t(n), uint64_t(k), uint64_t(w_ld), BN))
+      return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
+    mode = MODE_BF16;
+  } else if (decode_once(fmt, M)) {
     // Decode the weights once into the workspace (bf16 [n, k]), then stream
     // them with TMA like the activations.
     char* wb = ws + 256 + align256(size_t(M) * size_t(k) * 2);
@@ -1500,4 +1528,13 @@ extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor
                                                    n > 1 ? out->strides[0] : cout, out->dtype);
   }
   return check_launch(op);
+}
+
+extern "C" int l3d_linear_ex(const l3d_tensor* x, const l3d_tensor* weight, const l3d_tensor* bias,
+                             int act, const l3d_tensor* residual, const l3d_tensor* gate,
+                             const l3d_tensor* y, void* workspace, size_t workspace_bytes,
+                             l3d_stream stream) {
+  if (!weight) return fail(L3D_E_NULL, "l3d_linear_ex: weight is required");
+  return run_dequant_linear(x, nullptr, 0, 0, 0, bias, act, residual, gate, y, workspace,
+                            workspace_bytes, stream, "l3d_linear_ex", weight);
 }

@@ -335,6 +335,33 @@ class QMatMul:
     __call__ = forward
 
 
+_LIN_WS = {}
+
+
+def linear(x, weight, bias=None, act=None, residual=None, gate=None, out=None, out_dtype=None):
+    """candle_nn::Linear::forward / ops::mul_mat_add on a bf16 [n, k] weight
+    (crate/runtime/nn_blocks.rs:82,179-195) on the tensor cores, with the
+    block's next element-wise ops in the GEMM epilogue:
+    y = residual + gate * act(x . W^T + bias) (act "gelu" (tanh), "gelu_erf",
+    "silu"; `out` may be `residual`)."""
+    _check_cuda(x, weight, bias, residual, gate, out)
+    n, k = weight.shape
+    x2 = x.reshape(-1, k)
+    if out is not None:
+        y = out.reshape(-1, n)
+    else:
+        y = torch.empty((x2.shape[0], n), dtype=out_dtype or x.dtype, device=x.device)
+    need = _lib.lib().l3d_linear_workspace_size(x2.shape[0], n, k)
+    ws = _LIN_WS.get(x.device)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=x.device)
+        _LIN_WS[x.device] = ws
+    r2 = None if residual is None else residual.reshape(-1, n)
+    call("l3d_linear_ex", ref(desc(x2)), ref(desc(weight)), ref(desc(bias)), ACT_CODES[act],
+         ref(desc(r2)), ref(desc(gate)), ref(desc(y)), ws.data_ptr(), ws.numel(), _s(x))
+    return y.reshape(*x.shape[:-1], n)
+
+
 # ------------------------------------------------------------------- sparse
 def sparse_neighbor_pairs(coords):
     """CoordMap + 27 per-offset neighbour lists (crate/runtime/trellis2_sparse.rs:68-106,

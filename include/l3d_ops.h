@@ -304,6 +304,22 @@ int l3d_dequant_linear_ex(const l3d_tensor* x, const void* wq, int fmt, int64_t 
                           const l3d_tensor* gate, const l3d_tensor* y, void* workspace,
                           size_t workspace_bytes, l3d_stream stream);
 
+/* Workspace bytes for l3d_linear_ex with m rows. */
+size_t l3d_linear_workspace_size(int64_t m, int64_t n, int64_t k);
+
+/* Dense linear with the same fused epilogue as l3d_dequant_linear_ex:
+ *   y = residual + gate * act(x . W^T + bias)
+ * W: BF16 [n, k], row-major with 16-byte aligned rows (k a multiple of 8),
+ * used as is (bf16 operands, f32 accumulation on the tensor cores).  Replaces
+ * candle_nn::Linear::forward / ops::mul_mat_add on unquantised weights
+ * (crate/runtime/nn_blocks.rs:82,179-195) followed by the element-wise ops of
+ * the blocks: Mlp fc1 + gelu_erf (crate/runtime/nn_blocks.rs:219-236), the
+ * LayerScale residual x + ls * proj(..) (crate/runtime/nn_blocks.rs:210-214,
+ * crate/runtime/vggt.rs:118-121) as residual = x, gate = ls. */
+int l3d_linear_ex(const l3d_tensor* x, const l3d_tensor* weight, const l3d_tensor* bias, int act,
+                  const l3d_tensor* residual, const l3d_tensor* gate, const l3d_tensor* y,
+                  void* workspace, size_t workspace_bytes, l3d_stream stream);
+
 /* ---- next row: submanifold sparse conv 3x3x3 ------------------------------------ */
 
 /* Dense neighbour table of a coordinate set: nbr[i, k] = row of coord_i +

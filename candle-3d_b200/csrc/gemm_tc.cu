@@ -275,6 +275,44 @@ __device__ __forceinline__ void dequant_tile(const Params& p, const uint8_t* raw
   }
 }
 
+// v[i] += bias[col0 + i] for NC columns: 16-byte loads through the read-only
+// path when the chunk lies inside N and the bias is 16-byte aligned (f32 or
+// bf16), else one element at a time (columns past N are left alone).
+template <int NC>
+__device__ __forceinline__ void add_bias(const Params& p, int col0, float (&v)[NC]) {
+  if (col0 + NC <= p.N && p.bias_vec) {
+    if (p.bias_dtype == L3D_F32) {
+      const float4* b4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col0);
+#pragma unroll
+      for (int q = 0; q < NC / 4; ++q) {
+        const float4 t = __ldg(b4 + q);
+        v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
+      }
+    } else {
+      const uint4* b8 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.bias) + col0);
+#pragma unroll
+      for (int q = 0; q < NC / 8; ++q) {
+        const uint4 t = __ldg(b8 + q);
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[8 * q + 2 * e] += __uint_as_float(w[e] << 16);
+          v[8 * q + 2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int col = col0 + i;
+    if (col < p.N)
+      v[i] += p.bias_dtype == L3D_F32
+                  ? __ldg(static_cast<const float*>(p.bias) + col)
+                  : __uint_as_float(uint32_t(__ldg(static_cast<const unsigned short*>(p.bias) + col)) << 16);
+  }
+}
+
 // Gather the 128 x 64 A tile of (m0, kb) into the K-major SW128 layout (row r
 // at r * 128 bytes, its 16-byte chunk j at chunk j ^ (r % 8)).  256 threads,
 // 4 chunks each: thread t takes chunk t % 8 of rows t / 8 + 32 i; src[] holds
@@ -517,24 +555,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = b2[i]; }
           }
-          if (p.bias) {
-            if (col0 + EPI_COLS <= p.N && p.bias_dtype == L3D_F32 && p.bias_vec) {
-              const float4* b4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col0);
-#pragma unroll
-              for (int q = 0; q < EPI_COLS / 4; ++q) {
-                const float4 t = __ldg(b4 + q);
-                v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < EPI_COLS; ++i) {
-                const int col = col0 + i < p.N ? col0 + i : p.N - 1;
-                v[i] += p.bias_dtype == L3D_F32
-                            ? __ldg(static_cast<const float*>(p.bias) + col)
-                            : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[col]);
-              }
-            }
-          }
+          if (p.bias) add_bias<EPI_COLS>(p, col0, v);
           if (tres) {
             if (p.act) {
               // In two halves of 32 columns (fewer live temporaries).
@@ -677,16 +698,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(taddr + uint32_t(c), v);
         const int col0 = n0 + c;
         if (row < rows_m && col0 < p.N) {
-          if (p.bias) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int col = col0 + i;
-              if (col < p.N)
-                v[i] += p.bias_dtype == L3D_F32
-                            ? __ldg(static_cast<const float*>(p.bias) + col)
-                            : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[col]);
-            }
-          }
+          if (p.bias) add_bias<32>(p, col0, v);
           if (p.act || p.res) epi_post<32>(p, row, col0, v);
           if (p.y_dtype == L3D_BF16) {
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + int64_t(row) * p.y_ld + col0;

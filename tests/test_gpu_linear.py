@@ -16,15 +16,17 @@ from test_gpu_qlinear import _act_ref
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,N,K,act,res,gate,ydt,wview", [
-    (700, 1024, 1536, "gelu_erf", False, False, "bf16", False),   # VGGT fc1 + GELU-erf
-    (600, 768, 512, "gelu", False, False, "f32", False),
-    (700, 1536, 1024, None, True, True, "bf16", False),           # x += ls * proj(h), in place
-    (300, 300, 256, "silu", True, False, "f32", False),           # N tail
-    (37, 520, 1000, None, True, True, "bf16", False),             # small M, N and K tails
-    (256, 384, 512, None, False, False, "bf16", True),            # weight = rows of a wider matrix
+@pytest.mark.parametrize("M,N,K,act,res,gate,ydt,wview,bdt", [
+    (700, 1024, 1536, "gelu_erf", False, False, "bf16", False, "f32"),  # VGGT fc1 + GELU-erf
+    (600, 768, 512, "gelu", False, False, "f32", False, "f32"),
+    (700, 1536, 1024, None, True, True, "bf16", False, "f32"),          # x += ls * proj(h), in place
+    (300, 300, 256, "silu", True, False, "f32", False, "f32"),          # N tail
+    (37, 520, 1000, None, True, True, "bf16", False, "f32"),            # small M, N and K tails
+    (256, 384, 512, None, False, False, "bf16", True, "f32"),           # weight = rows of a wider matrix
+    (700, 1024, 1024, "gelu_erf", False, False, "bf16", False, "bf16"),  # bf16 bias (the stacks' dtype)
+    (300, 300, 256, None, False, False, "f32", False, "bf16"),          # bf16 bias with an N tail
 ])
-def test_linear_fused_epilogue(ops, dev, M, N, K, act, res, gate, ydt, wview):
+def test_linear_fused_epilogue(ops, dev, M, N, K, act, res, gate, ydt, wview, bdt):
     import torch
 
     r = rng(300 + M + N)
@@ -33,10 +35,12 @@ def test_linear_fused_epilogue(ops, dev, M, N, K, act, res, gate, ydt, wview):
                              .astype(np.float32)).to(dev).to(torch.bfloat16)
     w = wfull[:, :K]
     b = torch.from_numpy((0.1 * r.standard_normal(N)).astype(np.float32)).to(dev)
+    if bdt == "bf16":
+        b = b.to(torch.bfloat16)
     xv = x.float().cpu().numpy().astype(np.float64)
     wv = w.float().cpu().numpy().astype(np.float64)
     tdt = torch.float32 if ydt == "f32" else torch.bfloat16
-    z = xv @ wv.T + b.cpu().numpy()
+    z = xv @ wv.T + b.float().cpu().numpy()
     bound = 1.2 * (2e-5 * (np.abs(xv) @ np.abs(wv).T)) + 1e-6
     ref = _act_ref(act, z)
     kw = {"act": act}

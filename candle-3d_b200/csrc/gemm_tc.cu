@@ -51,7 +51,6 @@ constexpr int THREADS = (6 + N_DQ_WARPS) * 32;
 // 32 f32), written by TMA stores whole 128-byte lines at a time.
 constexpr int EPI_COLS = 64;
 constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 4;  // 8 KB
-constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
 // Operand modes.  MODE_RAW_TMA / MODE_RAW_LDG decode GGML blocks in the
 // prologue (3 stages of x + B + raw window); MODE_BF16 streams a bf16 copy of
@@ -66,17 +65,28 @@ constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 // tiles; a tile gathers its rows through the pair sources, multiplies by
 // W[k] and stores the f32 products (a later pass adds them per output row in
 // offset order).
-enum { MODE_RAW_TMA = 0, MODE_RAW_LDG = 1, MODE_BF16 = 2, MODE_GATHER = 3, MODE_PAIRS = 4 };
+// MODE_BF16_EPI8 is MODE_BF16 with eight epilogue warps (see EPI_WARPS).
+enum { MODE_RAW_TMA = 0, MODE_RAW_LDG = 1, MODE_BF16 = 2, MODE_GATHER = 3, MODE_PAIRS = 4,
+       MODE_BF16_EPI8 = 5 };
 template <int MODE>
 struct ModeCfg {
   static constexpr bool FUSED = MODE == MODE_RAW_TMA || MODE == MODE_RAW_LDG;  // decode W
   static constexpr bool PAIRS = MODE == MODE_PAIRS;
   static constexpr bool GATHER = MODE == MODE_GATHER || PAIRS;                 // gather A
   static constexpr bool WORKERS = FUSED || GATHER;  // warps 6.. build an operand
-  static constexpr int NST = FUSED ? 3 : 4;
+  static constexpr bool BF16W = MODE == MODE_BF16 || MODE == MODE_BF16_EPI8;  // bf16 W by TMA
+  // MODE_BF16_EPI8 gives the idle worker warps 6-9 to the epilogue: eight
+  // epilogue warps, each on half of the tile's columns, for one pipeline
+  // stage less.  It pays when an activation runs in the epilogue (the
+  // epilogue then bounds the kernel at small K); a plain GEMM keeps the
+  // fourth stage.
+  static constexpr int EPI_WARPS = MODE == MODE_BF16_EPI8 ? 8 : 4;
+  static constexpr int NST = FUSED ? 3 : MODE == MODE_BF16_EPI8 ? 3 : 4;
   static constexpr int RAW = FUSED ? RAW_BYTES : 0;
-  static constexpr int EPI = FUSED ? 0 : EPI_BYTES;  // fused modes store directly
-  static constexpr int SMEM = NST * (A_BYTES + B_BYTES + RAW) + EPI + 1024 + 256;
+  static constexpr int EPI = FUSED ? 0 : EPI_WARPS * EPI_WARP_BYTES;  // fused modes store directly
+  static constexpr int SMEM = NST * (A_BYTES + B_BYTES + RAW) + EPI + 1024 + 512;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(3 * NST + 7 + 2 * EPI_WARPS <= 512 / 8, "barrier area");
 };
 // Status word codes written by the kernel into the workspace header.
 constexpr int ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_TMEM = 3, ST_TIMEOUT_RAW = 4;
@@ -378,7 +388,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* tempty = bars + 3 * STAGES + 2;        // [2] epilogue -> MMA
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
-  uint64_t* rbars = bars + 3 * STAGES + 7;         // [4][2] residual TMA -> epilogue warp
+  uint64_t* rbars = bars + 3 * STAGES + 7;         // [EPI_WARPS][2] residual TMA -> epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // MODE_PAIRS: segment boundaries (in tiles) and pair counts per offset.
@@ -405,9 +415,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], ModeCfg<MODE>::EPI_WARPS);
     }
-    for (int w = 0; w < 8; ++w) mbar_init(&rbars[w], 1);
+    for (int w = 0; w < 2 * ModeCfg<MODE>::EPI_WARPS; ++w) mbar_init(&rbars[w], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -432,7 +442,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
           mbar_expect_tx(&lfull[stage], MODE == MODE_RAW_TMA ? A_BYTES + RAW_BYTES
-                                        : MODE == MODE_BF16  ? A_BYTES + B_BYTES
+                                        : ModeCfg<MODE>::BF16W ? A_BYTES + B_BYTES
                                         : GATHER             ? B_BYTES  // gather / pairs
                                                              : A_BYTES);
           if constexpr (GATHER) {
@@ -448,7 +458,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int c0 = ((kb * p.bpt) >> 4) << 3;
             tma_load_2d(sr + stage * RAWB, &map_w, &lfull[stage], c0, n0);
           }
-          if constexpr (MODE == MODE_BF16) {
+          if constexpr (ModeCfg<MODE>::BF16W) {
             tma_load_2d(sb + stage * B_BYTES, &map_w, &lfull[stage], kb * BK, n0);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -489,9 +499,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         umma_commit(&tfull[acc]);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + ModeCfg<MODE>::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // Columns [c_lo, c_hi) of each tile: all of them with four epilogue
+    // warps; with eight, warps 2-5 take the first half and 6-9 the second.
+    constexpr int EPI_SPAN = ModeCfg<MODE>::EPI_WARPS == 8 ? BN / 2 : BN;
+    const int c_lo = ((warp - 2) >> 2) * EPI_SPAN, c_hi = c_lo + EPI_SPAN;
+    const int ci_end = c_hi / EPI_COLS;  // chunk index past this warp's columns
     int local = 0;
     // TMA-store epilogue staging, 8 KB per epilogue warp.  Without a residual,
     // bf16 chunks (32 x 64 = 4 KB) alternate between its two halves (a store
@@ -524,7 +539,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // The tile's first residual chunk loads while the MMA still works.
         if (p.tma_store && p.res && p.res_tma && lane == 0) {
           if (f32o) bulk_wait_read0();  // in-place staging: the last store has read it
-          issue_res(m0, n0, 0);
+          issue_res(m0, n0, c_lo / EPI_COLS);
         }
       }
       if (!mbar_wait_idle(&tfull[acc], acc_phase, abort_flag, p.status, ST_TIMEOUT_TMEM)) break;
@@ -540,7 +555,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool tres = p.res && p.res_tma;
         bool eok = true;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += EPI_COLS) {
+        for (int c = c_lo; c < c_hi; c += EPI_COLS) {
           const int col0 = n0 + c;
           if (col0 >= p.N) break;  // warp-uniform; later chunks are past N too
           const int ci = c / EPI_COLS;
@@ -615,7 +630,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
               // Every lane has read the residual half: load the next chunk.
               __syncwarp();
-              if (lane == 0 && ci + 1 < BN / EPI_COLS) issue_res(m0, n0, ci + 1);
+              if (lane == 0 && ci + 1 < ci_end) issue_res(m0, n0, ci + 1);
             }
           }
           if (f32 && !tres) {
@@ -679,7 +694,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_store_2d(&map_y, obuf, col0, m0 + quarter * 32);
             if (f32 && col0 + 32 < p.N) tma_store_2d(&map_y, obuf + 4096, col0 + 32, m0 + quarter * 32);
             bulk_commit();
-            if (tres && f32 && ci + 1 < BN / EPI_COLS) {
+            if (tres && f32 && ci + 1 < ci_end) {
               bulk_wait_read0();  // in place: this store has read the staging
               issue_res(m0, n0, ci + 1);
             }
@@ -693,7 +708,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         continue;
       }
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = c_lo; c < c_hi; c += 32) {
         float v[32];
         tmem_ld32(taddr + uint32_t(c), v);
         const int col0 = n0 + c;
@@ -1079,7 +1094,7 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
     // Dense bf16 weights: streamed by TMA as they are.
     if (!make_map_x(&map_w, wq, uint64_t(n), uint64_t(k), uint64_t(w_ld), BN))
       return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
-    mode = MODE_BF16;
+    mode = act != ACT_NONE ? MODE_BF16_EPI8 : MODE_BF16;
   } else if (decode_once(fmt, M)) {
     // Decode the weights once into the workspace (bf16 [n, k]), then stream
     // them with TMA like the activations.
@@ -1088,7 +1103,7 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
     if (rc) return rc;
     if (!make_map_x(&map_w, wb, uint64_t(n), uint64_t(k), uint64_t(k), BN))
       return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the decoded weights", op);
-    mode = MODE_BF16;
+    mode = act != ACT_NONE ? MODE_BF16_EPI8 : MODE_BF16;
   } else {
     // The TMA window needs 16-byte aligned weight rows (k % 256 == 0).
     const bool raw_tma = (reinterpret_cast<uintptr_t>(wq) % 16 == 0) && (p.row_bytes % 16 == 0) &&
@@ -1119,6 +1134,10 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
       attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_BF16>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       ModeCfg<MODE_BF16>::SMEM);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_BF16_EPI8>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      ModeCfg<MODE_BF16_EPI8>::SMEM);
   });
   if (attr_err != cudaSuccess)
     return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
@@ -1130,6 +1149,9 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
       break;
     case MODE_RAW_LDG:
       qgemm_kernel<MODE_RAW_LDG><<<grid, THREADS, ModeCfg<MODE_RAW_LDG>::SMEM, s>>>(map_x, map_w, map_y, map_r, p);
+      break;
+    case MODE_BF16_EPI8:
+      qgemm_kernel<MODE_BF16_EPI8><<<grid, THREADS, ModeCfg<MODE_BF16_EPI8>::SMEM, s>>>(map_x, map_w, map_y, map_r, p);
       break;
     default:
       qgemm_kernel<MODE_BF16><<<grid, THREADS, ModeCfg<MODE_BF16>::SMEM, s>>>(map_x, map_w, map_y, map_r, p);

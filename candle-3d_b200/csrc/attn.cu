@@ -249,6 +249,19 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   const int ntv = int((p.nq - q0 + BQ - 1) / BQ) < NT ? int((p.nq - q0 + BQ - 1) / BQ) : NT;
   // MMA warps with work: each commits the release of every K / V stage.
   const int nmma = C::SEP_P ? ntv : 1;
+  // Key tile j (K and V, 128 keys) into ring stage j % STAGES (thread 0).
+  auto load_kv = [&](int j) {
+    const int s = j % C::STAGES;
+    mbar_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
+    uint8_t* kt = sk + s * C::K_BYTES;
+    for (int dc = 0; dc < C::DC; ++dc)
+      tma_load_4d(kt + dc * (BKV * 128), &map_k, &kv_full[s], dc * 64, p.k_hn ? h : j * BKV,
+                  p.k_hn ? j * BKV : h, b);
+    uint8_t* vt = sv + s * C::V_BYTES;
+    for (int dc = 0; dc < C::DC; ++dc)
+      tma_load_4d(vt + dc * (BKV * 128), &map_v, &kv_full[s], dc * 64, p.v_hn ? h : j * BKV,
+                  p.v_hn ? j * BKV : h, b);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -264,6 +277,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // The Q tiles and the first key tiles start loading before the TMEM
+    // allocation and the block barrier (the producer issues the rest).
+    mbar_expect_tx(q_full, ntv * C::Q_BYTES);
+    for (int t = 0; t < ntv; ++t)
+      for (int dc = 0; dc < C::DC; ++dc) {
+        const int row = q0 + t * BQ;
+        tma_load_4d(sq + t * C::Q_BYTES + dc * (BQ * 128), &map_q, q_full, dc * 64,
+                    p.q_hn ? h : row, p.q_hn ? row : h, b);
+      }
+    for (int j = 0; j < nkv && j < C::STAGES; ++j) load_kv(j);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -278,28 +301,13 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // (the Q tiles and the first STAGES key tiles were issued at set-up)
     if (lane == 0) {
-      mbar_expect_tx(q_full, ntv * C::Q_BYTES);
-      for (int t = 0; t < ntv; ++t)
-        for (int dc = 0; dc < C::DC; ++dc) {
-          const int row = q0 + t * BQ;
-          tma_load_4d(sq + t * C::Q_BYTES + dc * (BQ * 128), &map_q, q_full, dc * 64,
-                      p.q_hn ? h : row, p.q_hn ? row : h, b);
-        }
-      for (int j = 0; j < nkv && !*abort_flag; ++j) {
+      for (int j = C::STAGES; j < nkv && !*abort_flag; ++j) {
         const int s = j % C::STAGES;
-        if (j >= C::STAGES &&
-            !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, ST_TIMEOUT))
+        if (!mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, ST_TIMEOUT))
           break;
-        mbar_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
-        uint8_t* kt = sk + s * C::K_BYTES;
-        for (int dc = 0; dc < C::DC; ++dc)
-          tma_load_4d(kt + dc * (BKV * 128), &map_k, &kv_full[s], dc * 64, p.k_hn ? h : j * BKV,
-                      p.k_hn ? j * BKV : h, b);
-        uint8_t* vt = sv + s * C::V_BYTES;
-        for (int dc = 0; dc < C::DC; ++dc)
-          tma_load_4d(vt + dc * (BKV * 128), &map_v, &kv_full[s], dc * 64, p.v_hn ? h : j * BKV,
-                      p.v_hn ? j * BKV : h, b);
+        load_kv(j);
       }
     }
   } else if (warp <= C::NMMA) {

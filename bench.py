@@ -9,12 +9,19 @@ Algorithmic bytes: each op reads and writes every activation element once
 (bf16: 4 B/elem/op, 12 B/elem/step); parameters, positions and coordinates are
 not counted.  `value` is the whole-job layer-op GB/s (all ranks' bytes / max
 rank time); `e2e` is the same metric through the C ABI with the input copied
-from pinned host memory and the output copied back inside the timed region.
+from pinned host memory and the output copied back inside the timed region
+(row chunks pipelined over three streams).  `parity` checks the first rows of
+the timed output against the CPU oracle.
+
+The same line carries the metric's other half, `block_stack`: tokens/s of ONE
+VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
+head-parallel), and at N = 1 `config1_fp32`, the f32 micro-suite per op.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Multi-GPU: launched by torch.distributed.run, one rank per GPU; every rank
-owns its own rows (weak scaling, no data-path collective); the final NCCL
-all-gather of the outputs is timed separately and reported as `allgather`.
+owns its own rows (weak scaling, no data-path collective in `value`); the
+final NCCL all-gather of the outputs, overlapped chunk by chunk with the
+chain, is timed as `allgather` (with its gather-inclusive GB/s).
 """
 from __future__ import annotations
 
@@ -45,10 +52,21 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--rows", type=int, default=1 << 20, help="token rows per GPU")
     ap.add_argument("--channels", type=int, default=2048, choices=[1024, 1536, 2048])
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help="end-to-end steps (default: --steps)")
+    ap.add_argument("--e2e-chunks", type=int, default=32,
+                    help="row chunks of the end-to-end copy/compute pipeline")
+    ap.add_argument("--gather-chunks", type=int, default=16,
+                    help="N > 1: row chunks of the overlapped final all-gather")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-stack", action="store_true",
+                    help="chain workload: skip the VGGT one-scene block_stack sub-record")
+    ap.add_argument("--no-config1", action="store_true",
+                    help="chain workload: skip the config-1 f32 micro-suite sub-record")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
+    ap.add_argument("--check-rows", type=int, default=8192,
+                    help="rows of the timed output checked against the oracle (0: no check)")
     ap.add_argument("--qfmt", default="q8_0", choices=["q8_0", "q4_k", "q5_k", "q6_k"],
                     help="qlinear workload: weight format (q8_0 is config 4's)")
     ap.add_argument("--workload", default="chain",
@@ -181,7 +199,8 @@ def make_inputs(T, C, seed, dev):
 
 
 class Chain:
-    """The three fused kernels of one step, on preallocated buffers."""
+    """The three fused kernels of one step, on preallocated buffers.  Every op
+    can run on a row range (the chunked end-to-end and gather pipelines)."""
 
     def __init__(self, ops, inp, T, C):
         import torch
@@ -195,51 +214,118 @@ class Chain:
         self.b = torch.empty((T, C), dtype=torch.bfloat16, device=dev)
         self.names = ["layer_norm_modulate", "qk_norm_rope", "gelu_tanh"]
 
-    def op(self, i, x=None):
-        ops, inp, T, H, D = self.ops, self.inp, self.T, self.H, self.D
-        x = inp["x"] if x is None else x
+    def op(self, i, x=None, rows=None):
+        ops, inp, H, D = self.ops, self.inp, self.H, self.D
+        r0, r1 = (0, self.T) if rows is None else rows
+        T = r1 - r0
+        x = (inp["x"] if x is None else x)[r0:r1]
+        a, b = self.a[r0:r1], self.b[r0:r1]
         if i == 0:
-            self._lnm(x)
+            self._lnm(x, a)
         elif i == 1:
             if self.kind == "rope2d":
-                q = self.a.view(1, T, H, D).permute(0, 2, 1, 3)
-                qo = self.b.view(1, T, H, D).permute(0, 2, 1, 3)
-                w, b = inp["params"]
-                ops.qk_layernorm_rope2d(q, None, w, b, None, None, 1e-5, inp["aux"], 100.0, q_out=qo)
+                q = a.view(1, T, H, D).permute(0, 2, 1, 3)
+                qo = b.view(1, T, H, D).permute(0, 2, 1, 3)
+                w, bb = inp["params"]
+                ops.qk_layernorm_rope2d(q, None, w, bb, None, None, 1e-5, inp["aux"][:, r0:r1],
+                                        100.0, q_out=qo)
             else:
-                ops.qk_l2norm_rope3d(self.a.view(1, T, H, D), inp["params"][0], inp["aux"], 10000.0,
-                                     out=self.b.view(1, T, H, D))
+                ops.qk_l2norm_rope3d(a.view(1, T, H, D), inp["params"][0], inp["aux"][r0:r1],
+                                     10000.0, out=b.view(1, T, H, D))
         else:
-            self._gelu()
+            self._gelu(b, a)
 
-    def _lnm(self, x):
+    def _lnm(self, x, out):
         from candle3d_b200 import _lib
         from candle3d_b200._lib import desc, ref
 
         _lib.call("l3d_layer_norm_modulate", ref(desc(x)), None, None, ref(desc(self.inp["shift"])),
-                  ref(desc(self.inp["scale"])), None, 0, 1e-6, ref(desc(self.a)),
+                  ref(desc(self.inp["scale"])), None, 0, 1e-6, ref(desc(out)),
                   _lib.stream_handle(x.device))
 
-    def _gelu(self):
+    def _gelu(self, x, out):
         from candle3d_b200 import _lib
         from candle3d_b200._lib import desc, ref
 
-        _lib.call("l3d_gelu_tanh", ref(desc(self.b)), ref(desc(self.a)),
-                  _lib.stream_handle(self.a.device))
+        _lib.call("l3d_gelu_tanh", ref(desc(x)), ref(desc(out)), _lib.stream_handle(x.device))
 
-    def step(self, x=None):
+    def step(self, x=None, rows=None):
         for i in range(3):
-            self.op(i, x)
+            self.op(i, x, rows)
         return self.a  # y3
 
 
+def chunk_bounds(T, chunks):
+    step = -(-T // chunks)
+    return [(r, min(T, r + step)) for r in range(0, T, step)]
+
+
+class E2EPipeline:
+    """One step end to end through the C ABI with host buffers: row chunks
+    flow pinned host -> device -> chain -> pinned host on three streams, so the
+    host-to-device copy of chunk i + 1, the chain on chunk i and the
+    device-to-host copy of chunk i - 1 run at once (both PCIe directions
+    busy).  Events order each chunk's copies and kernels, also across steps."""
+
+    def __init__(self, chain, hx, haux, hy, chunks):
+        import torch
+
+        self.chain, self.hx, self.haux, self.hy = chain, hx, haux, hy
+        self.dx = torch.empty_like(chain.inp["x"])
+        self.bounds = chunk_bounds(chain.T, chunks)
+        self.h2d, self.cmp, self.d2h = (torch.cuda.Stream() for _ in range(3))
+        n = len(self.bounds)
+        self.ev_in, self.ev_out, self.ev_done = ([torch.cuda.Event() for _ in range(n)]
+                                                 for _ in range(3))
+
+    def _aux(self, t, r0, r1):
+        return t[:, r0:r1] if self.chain.kind == "rope2d" else t[r0:r1]
+
+    def step(self):
+        import torch
+
+        aux = self.chain.inp["aux"]
+        for i, (r0, r1) in enumerate(self.bounds):
+            with torch.cuda.stream(self.h2d):
+                self.h2d.wait_event(self.ev_out[i])     # the last step's chain read dx
+                self.dx[r0:r1].copy_(self.hx[r0:r1], non_blocking=True)
+                self._aux(aux, r0, r1).copy_(self._aux(self.haux, r0, r1), non_blocking=True)
+                self.ev_in[i].record(self.h2d)
+            with torch.cuda.stream(self.cmp):
+                self.cmp.wait_event(self.ev_in[i])
+                self.cmp.wait_event(self.ev_done[i])    # the last step's copy-out read a
+                self.chain.step(self.dx, (r0, r1))
+                self.ev_out[i].record(self.cmp)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.ev_out[i])
+                self.hy[r0:r1].copy_(self.chain.a[r0:r1], non_blocking=True)
+                self.ev_done[i].record(self.d2h)
+
+    def timed(self, steps, barrier, max_over_ranks):
+        import torch
+
+        self.step()  # warm
+        torch.cuda.synchronize()
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(self.h2d)
+        for _ in range(steps):
+            self.step()
+        a1.record(self.d2h)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(a0.elapsed_time(a1))
+
+
 def chain_reference_cpu(orc, host, C):
-    """The same chain on the CPU oracle (f32 arithmetic on the bf16 inputs)."""
+    """The same chain on the CPU oracle: f32 arithmetic on the bf16 inputs, each
+    op's output rounded to bf16 as the bf16 tensors between Candle ops hold it."""
     H, D, kind = head_cfg(C)
     x = host["x"].float().numpy()
     T = x.shape[0]
     y1 = orc.layer_norm_modulate(x.reshape(1, T, C), shift=host["shift"].float().numpy(),
                                  scale=host["scale"].float().numpy(), eps=1e-6)
+    y1 = orc.round_bf16(y1)
     if kind == "rope2d":
         w, b = (p.float().numpy() for p in host["params"])
         q = np.ascontiguousarray(y1.reshape(1, T, H, D).transpose(0, 2, 1, 3))
@@ -249,7 +335,7 @@ def chain_reference_cpu(orc, host, C):
     else:
         y2 = orc.qk_l2norm_rope3d(y1.reshape(1, T, H, D), host["params"][0].numpy(),
                                   host["aux"].numpy().astype(np.int64), 10000.0)
-    return orc.gelu_tanh(y2.reshape(T, C))
+    return orc.gelu_tanh(orc.round_bf16(np.ascontiguousarray(y2.reshape(T, C))))
 
 
 def time_cpu_chain(orc, C, rows, seed, min_seconds=10.0):
@@ -263,6 +349,232 @@ def time_cpu_chain(orc, C, rows, seed, min_seconds=10.0):
         if el >= min_seconds:
             break
     return 12.0 * rows * C * n / el / 1e9, n, el
+
+
+# ----------------------------------------------------- config 1 (fp32 suite)
+def config1_record(ops, dev, orc=None, launches=20):
+    """BASELINE config 1 at the reference's own precision (f32): x [2, 4096,
+    1024] ~ N(0, 1), gamma ~ N(1, .02), beta ~ N(0, .02), eps 1e-6; shift /
+    scale / gate [2, 1024] ~ N(0, .1); q, k [2, 16, 4096, 64]; positions of a
+    64 x 64 grid, theta 100; GELU-tanh on [2, 4096, 4096].  Each op: the mean
+    CUDA-event time of `launches` launches rotating through enough input sets
+    that the sets exceed twice the 126 MB L2, its algorithmic GB/s (every
+    activation read and written once) and fraction of the measured HBM peak;
+    with `orc`, the CPU oracle's time for the same op on all host threads."""
+    import math
+
+    import torch
+
+    peak, peak_kind = measured_peaks()
+    g = torch.Generator().manual_seed(20261201)
+    f32 = torch.float32
+    B, N, C, H, D = 2, 4096, 1024, 16, 64
+
+    def rn(*shape, std=1.0, mean=0.0):
+        return mean + std * torch.randn(*shape, generator=g, dtype=f32)
+
+    w, b = rn(C, std=0.02, mean=1.0), rn(C, std=0.02)
+    shift, scale, gate = rn(B, C, std=0.1), rn(B, C, std=0.1), rn(B, C, std=0.1)
+    qw, qb, kw, kb = rn(D, std=0.02, mean=1.0), rn(D, std=0.02), rn(D, std=0.02, mean=1.0), rn(D, std=0.02)
+    pos = ops.position_getter(B, 64, 64, "cpu").to(torch.int32)
+    xs_h = rn(B, N, C)
+    dv = lambda t: t.to(dev)  # noqa: E731
+    W, Bb, SH, SC, G = map(dv, (w, b, shift, scale, gate))
+    QW, QB, KW, KB, P = map(dv, (qw, qb, kw, kb, pos))
+    e = B * N * C
+    # name: (algorithmic bytes per launch, make one input set, launch on a set)
+    suite = {
+        "layer_norm": (8 * e, lambda: (dv(rn(B, N, C)),),
+                       lambda t: ops.layer_norm(t[0], W, Bb, eps=1e-6)),
+        "layer_norm_modulate_gate": (8 * e, lambda: (dv(rn(B, N, C)),),
+                                     lambda t: ops.layer_norm_modulate(t[0], SH, SC, gate=G, eps=1e-6)),
+        "gated_residual": (12 * e, lambda: (dv(rn(B, N, C)), dv(rn(B, N, C))),
+                           lambda t: ops.gated_residual(t[0], t[1], G)),
+        "qk_layernorm_rope2d": (2 * 8 * e, lambda: (dv(rn(B, H, N, D)), dv(rn(B, H, N, D))),
+                                lambda t: ops.qk_layernorm_rope2d(t[0], t[1], QW, QB, KW, KB, 1e-6,
+                                                                  P, 100.0)),
+        "qk_rms_norm_heads": (2 * 8 * e, lambda: (dv(rn(B, H, N, D)), dv(rn(B, H, N, D))),
+                              lambda t: (ops.rms_norm_heads(t[0], QW, 1e-6),
+                                         ops.rms_norm_heads(t[1], KW, 1e-6))),
+        "gelu_tanh": (8 * 4 * e, lambda: (dv(rn(B, N, 4 * C)),), lambda t: ops.gelu(t[0])),
+    }
+    stream = torch.cuda.current_stream(dev)
+    rec = {"shapes": "x [2,4096,1024], q/k [2,16,4096,64], GELU [2,4096,4096], f32",
+           "peak": peak, "peak_source": peak_kind, "ops": {}}
+    for name, (nbytes, make, run) in suite.items():
+        nsets = max(2, math.ceil(2 * 126e6 / nbytes))
+        sets = [make() for _ in range(nsets)]
+        outs = [None] * nsets  # outputs kept alive per set, so they rotate too
+        for i in range(3):
+            outs[i % nsets] = run(sets[i % nsets])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(launches):
+            outs[i % nsets] = run(sets[i % nsets])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / launches
+        gbs = nbytes / (ms / 1e3) / 1e9
+        rec["ops"][name] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
+                            "bytes": int(nbytes), "input_sets": nsets}
+        del sets, outs
+    rec["launches"] = 7 * launches  # six ops, the RMSNorm-heads op launches once per tensor
+    if orc is not None:
+        cs, sn = orc.rope2d_tables(pos.numpy().astype(np.int64), 100.0, D)
+        x, x2 = xs_h.numpy(), rn(B, N, C).numpy()
+        q, k = rn(B, H, N, D).numpy(), rn(B, H, N, D).numpy()
+        xg = rn(B, N, 4 * C).numpy()
+        cpu_ops = {
+            "layer_norm": lambda: orc.layer_norm(x, w.numpy(), b.numpy(), 1e-6),
+            "layer_norm_modulate_gate": lambda: orc.layer_norm_modulate(
+                x, shift=shift.numpy(), scale=scale.numpy(), gate=gate.numpy(), eps=1e-6),
+            "gated_residual": lambda: orc.gated_residual(x, x2, gate.numpy()),
+            "qk_layernorm_rope2d": lambda: (orc.layernorm_rope2d(q, qw.numpy(), qb.numpy(), 1e-6, cs, sn),
+                                            orc.layernorm_rope2d(k, kw.numpy(), kb.numpy(), 1e-6, cs, sn)),
+            "qk_rms_norm_heads": lambda: (orc.rms_norm_heads(q, qw.numpy(), 1e-6),
+                                          orc.rms_norm_heads(k, kw.numpy(), 1e-6)),
+            "gelu_tanh": lambda: orc.gelu_tanh(xg),
+        }
+        for name, fn in cpu_ops.items():
+            fn()
+            best = min(_seconds(fn) for _ in range(3))
+            rec["ops"][name]["cpu_ms"] = round(best * 1e3, 2)
+            rec["ops"][name]["cpu_GBps"] = round(rec["ops"][name]["bytes"] / best / 1e9, 2)
+        rec["cpu"] = {"cores": orc.num_threads(), "kind": "port",
+                      "what": "C oracle, best of 3 calls per op, all host threads"}
+    return rec
+
+
+def _seconds(fn):
+    t0 = time.perf_counter()
+    fn()
+    return time.perf_counter() - t0
+
+
+# ------------------------------------------------- config 2, one scene split
+def vggt_scene(args, world, rank, local, check=True):
+    """Config 2 (VGGT-1B aggregator): one scene of S = 8 views x 1374 tokens
+    through patch embedding, 24 frame + 24 global blocks and the final
+    all-gather of the block outputs, split across the `world` ranks (S / world
+    views per rank: frame blocks local, global blocks head-parallel through
+    two all-to-alls, shard.SceneSplit).  The process group must already be
+    initialised when world > 1.  Returns tokens/s of the one scene, the
+    achieved TFLOP/s per GPU against the sustained bf16 peak, end-to-end
+    tokens/s (pixels in from pinned host memory, gathered tokens out), and at
+    world > 1 the sharded-vs-single-GPU output difference (rank 0 reruns the
+    scene alone)."""
+    import torch
+
+    import __graft_entry__ as graft
+
+    pkg = graft.load_package()
+    from candle3d_b200 import blocks, shard
+
+    blocks.set_attention(args.attention)
+    ops = pkg.ops
+    dev = torch.device("cuda", local)
+    S, ph, C = 8, 37, 1024
+    N = 5 + ph * ph
+    if S % world:
+        return {"unavailable": f"{S} views do not split over {world} ranks"}
+    sl = S // world
+    v0 = rank * sl
+    split = shard.SceneSplit() if world > 1 else None
+    inp = vggt_inputs(dev, S)
+    agg = blocks.VggtAggregator(depth=24, device=dev)
+    special = torch.cat([inp["special"][:1], inp["special"][1:].expand(S - 1, 5, C)], 0)
+
+    def runner(views, nsplit):
+        lo, hi = views
+        fpos = blocks.VggtAggregator.positions(1, hi - lo, ph, ph, 5, dev)
+        gpos = fpos.reshape(1, (hi - lo) * N, 2)
+        sp = special[lo:hi]
+
+        def step(pixels):
+            tok = ops.patch_embed(pixels, inp["w"], inp["b"], inp["pos"], inp["cls"], inp["reg"], 14)
+            tokens = torch.cat([sp, tok[:, 5:]], 1)
+            out = agg.forward(tokens, fpos, gpos, hi - lo, split=nsplit)
+            return out.view((hi - lo) * N, C) if nsplit is None else nsplit.all_gather_rows(
+                out.view((hi - lo) * N, C))
+        return step
+
+    step = runner((v0, v0 + sl), split)
+    px = inp["pixels"][v0:v0 + sl].contiguous()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def maxr(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        out = step(px)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = step(px)
+    e1.record(stream)
+    barrier()
+    ms = maxr(e0.elapsed_time(e1)) / args.steps
+    tokens = S * N
+    flops = 24 * (2 * 24 * tokens * C * C + 4 * S * N * N * C + 4 * (S * N) ** 2 * C)
+    peak_tf = 1395.8
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak_tf = float(json.loads(pk.read_text()).get("bf16_tflops_sustained", peak_tf))
+    ach = flops / (ms / 1e3) / 1e12 / world
+    # End to end: this rank's views' pixels in from pinned host memory, the
+    # gathered scene tokens back out, every step.
+    hp = px.cpu().pin_memory()
+    dp = torch.empty_like(px)
+    hy = torch.empty((tokens, C), dtype=torch.bfloat16).pin_memory()
+    barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        dp.copy_(hp, non_blocking=True)
+        hy.copy_(step(dp), non_blocking=True)
+    a1.record(stream)
+    barrier()
+    ems = maxr(a0.elapsed_time(a1)) / args.steps
+    rec = {
+        "metric": "block-stack tokens/s", "value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s",
+        "ms_per_step": round(ms, 3), "steps": args.steps,
+        "workload": "config2 VGGT-1B aggregator, ONE scene: patch embed + 24 frame / 24 global "
+                    "blocks + final all-gather, S=8 views x 1374 tokens, dim 1024, 16 heads",
+        "parallelism": (f"scene split over {world} GPUs: {sl} view(s) per rank, global blocks "
+                        f"head-parallel ({16 // world} heads per rank, 2 NCCL all-to-alls)")
+                       if world > 1 else "single GPU",
+        "attention": args.attention,
+        "roofline": {"bound": "tensor", "achieved_per_gpu": round(ach, 1), "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": round(ach / peak_tf, 4),
+                     "flops_per_scene": float(flops)},
+        "e2e": {"value": round(tokens / (ems / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(hp.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
+    }
+    if world > 1 and check:
+        # The same scene on rank 0 alone (no split) against the gathered split output.
+        sharded = out.float()
+        if rank == 0:
+            single = runner((0, S), None)(inp["pixels"]).float()
+            torch.cuda.synchronize()
+            d = (sharded - single)
+            rel = float(d.norm() / single.norm())
+            rec["parity_vs_single_gpu"] = {"rel_l2": rel, "max_abs": float(d.abs().max()),
+                                           "tol": "rel L2 < 2e-2 (bf16 stack)", "ok": rel < 2e-2}
+        barrier()
+    return rec
 
 
 # -------------------------------------------------------------------- main
@@ -289,11 +601,11 @@ def vggt_inputs(dev, S=8, seed=20261201):
 
 
 class Replicas:
-    """The block stacks at N > 1: every rank runs its own scene on its own GPU
-    (a scene's tokens are coupled by global attention, so a scene is not
-    split); no collective touches the data.  Timed regions are bracketed by
-    an NCCL barrier and a device sync, and their times are the max over
-    ranks."""
+    """Process group and timing helpers of the block-stack workloads.  The
+    TripoSG and TRELLIS stacks run one scene per GPU at N > 1 (no collective
+    touches their data); the VGGT stack splits one scene (vggt_scene).  Timed
+    regions are bracketed by an NCCL barrier and a device sync, and their
+    times are the max over ranks."""
 
     def __init__(self, world, local):
         import torch
@@ -331,92 +643,30 @@ class Replicas:
 
 
 def run_vggt(args, world, rank, local):
-    """Config 2 stack: patch embedding (l3d_patch_embed) of S = 8 views, the
-    camera/register tokens, then 24 frame + 24 global VGGT blocks
-    (candle-3d_b200/blocks.py).  One step = one aggregator forward; the metric
-    is tokens/s (S * 1374 tokens per step)."""
+    """Config 2 stack alone: ONE VGGT scene per step, split across the ranks
+    (vggt_scene); the metric is tokens/s of that scene."""
     import torch
 
-    import __graft_entry__ as graft
-
-    pkg = graft.load_package()
-    from candle3d_b200 import blocks
-
-    blocks.set_attention(args.attention)
-    ops = pkg.ops
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    reps = Replicas(world, local)
-    S, ph = 8, 37
-    N = 5 + ph * ph
-    inp = vggt_inputs(dev, S)
-    agg = blocks.VggtAggregator(depth=24, device=dev)
-    fpos = blocks.VggtAggregator.positions(1, S, ph, ph, 5, dev)
-    gpos = fpos.reshape(1, S * N, 2)
-    special = torch.cat([inp["special"][:1], inp["special"][1:].expand(S - 1, 5, 1024)], 0)
-
-    def step(pixels):
-        tok = ops.patch_embed(pixels, inp["w"], inp["b"], inp["pos"], inp["cls"], inp["reg"], 14)
-        tokens = torch.cat([special, tok[:, 5:]], 1)
-        return agg.forward(tokens, fpos, gpos, S)
-
-    stream = torch.cuda.current_stream(dev)
-    for _ in range(max(args.warmup, 3)):
-        step(inp["pixels"])
-    reps.barrier()
+    reps = Replicas(world, local)  # process group + barrier / max helpers
     sampler = ClockSampler(local)
     sampler.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step(inp["pixels"])
-    e1.record(stream)
-    reps.barrier()
-    ms = reps.max(e0.elapsed_time(e1))
+    rec = vggt_scene(args, world, rank, local)
     clocks = sampler.stop()
-    tokens_step = S * N
-    value = world * tokens_step * args.steps / (ms / 1e3)
-    # Per frame/global block pair: linears 2 x 24 T C^2, attention 4 S N^2 C
-    # (frame) + 4 (S N)^2 C (global); 24 pairs (about 2.66e13 FLOP per step).
-    C = 1024
-    flops = 24 * (2 * 24 * tokens_step * C * C + 4 * S * N * N * C + 4 * (S * N) ** 2 * C)
-    peak_tf = 1402.3
-    pk = ROOT / "MEASURED_PEAKS.json"
-    if pk.exists():
-        peak_tf = float(json.loads(pk.read_text()).get("bf16_tflops_sustained", peak_tf))
-    ach = flops / (ms / args.steps / 1e3) / 1e12
-    # End to end: pixels from pinned host memory in, final tokens back out.
-    hp = inp["pixels"].cpu().pin_memory()
-    dp = torch.empty_like(inp["pixels"])
-    hy = torch.empty((S, N, 1024), dtype=torch.bfloat16).pin_memory()
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n2 = max(1, min(args.steps, 5))
-    reps.barrier()
-    a0.record(stream)
-    for _ in range(n2):
-        dp.copy_(hp, non_blocking=True)
-        hy.copy_(step(dp), non_blocking=True)
-    a1.record(stream)
-    reps.barrier()
-    ems = reps.max(a0.elapsed_time(a1))
     line = {
-        "metric": "block-stack tokens/s", "value": round(value, 1), "unit": "tokens/s",
+        "metric": "block-stack tokens/s", "value": rec["value"], "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": rec["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config 2 shapes)",
-        "config": {"workload": "config2 VGGT-1B aggregator: patch embed + 24 frame / 24 global "
-                               "blocks, S=8 views x 1374 tokens, dim 1024, 16 heads, MLP 4096",
-                   "parallelism": reps.parallelism("single GPU (global attention couples all views)"),
+        "config": {"workload": rec["workload"], "parallelism": rec["parallelism"],
                    "attention": args.attention, "baseline_metric": BASELINE_METRIC},
-        "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + SDPA + fused ops)",
-                     "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": round(ach / peak_tf, 4), "traffic": None},
-        "clocks": clocks,
-        "e2e": {"value": round(world * tokens_step * n2 / (ems / 1e3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(hp.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
+        "roofline": rec["roofline"], "clocks": clocks, "e2e": rec["e2e"],
+        "parity_vs_single_gpu": rec.get("parity_vs_single_gpu"),
     }
     if rank == 0:
         print(json.dumps(line))
+    del dev
     reps.close()
     return 0
 
@@ -814,7 +1064,6 @@ def main():
     bytes_step = 12.0 * T * C  # bf16: 3 ops x (read + write) x 2 B
     stream = torch.cuda.current_stream(dev)
 
-    # Parity spot check on a slice (rows processed identically as in the bench).
     for _ in range(max(args.warmup, 3)):
         chain.step()
     torch.cuda.synchronize()
@@ -836,6 +1085,9 @@ def main():
     ms = max_over_ranks(e0.elapsed_time(e1))
     clocks = sampler.stop() if sampler else None
     value = world * bytes_step * args.steps / (ms / 1e3) / 1e9
+    # The first rows of the last timed step's output, kept for the parity check.
+    check_rows = min(T, args.check_rows)
+    y_check = chain.a[:check_rows].float().cpu().numpy() if rank == 0 else None
 
     # ---- per-kernel durations (separate pass, events on the launch stream)
     per = {n: 0.0 for n in chain.names}
@@ -855,59 +1107,99 @@ def main():
     ach = 4.0 * T * C / (per[dom] / 1e3) / 1e9
     traffic = ncu_traffic(f"{dom}@{C}", T)
 
-    # ---- end to end through the C ABI with host buffers
+    # ---- end to end through the C ABI with host buffers: every step copies its
+    # input rows (and their positions / coordinates) from pinned host memory and
+    # its output rows back, chunk-pipelined over three streams.
     e2e = None
     if not args.no_e2e:
         hx = inp["x"].cpu().pin_memory()
         haux = inp["aux"].cpu().pin_memory()
         hy = torch.empty((T, C), dtype=torch.bfloat16).pin_memory()
-        dx = torch.empty_like(inp["x"])
-        n2 = max(1, args.e2e_steps)
-        for _ in range(1):
-            dx.copy_(hx, non_blocking=True)
-            inp["aux"].copy_(haux, non_blocking=True)
-            hy.copy_(chain.step(dx), non_blocking=True)
-        torch.cuda.synchronize()
-        barrier()
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
-        a0.record(stream)
-        for _ in range(n2):
-            dx.copy_(hx, non_blocking=True)
-            inp["aux"].copy_(haux, non_blocking=True)
-            y = chain.step(dx)
-            hy.copy_(y, non_blocking=True)
-        a1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        ems = max_over_ranks(a0.elapsed_time(a1))
+        pipe = E2EPipeline(chain, hx, haux, hy, args.e2e_chunks)
+        n2 = max(1, args.steps if args.e2e_steps is None else args.e2e_steps)
+        ems = pipe.timed(n2, barrier, max_over_ranks)
         e2e = {"value": round(world * bytes_step * n2 / (ems / 1e3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": int(hx.numel() * 2 + haux.numel() * 4),
                "d2h_bytes_per_step": int(hy.numel() * 2), "steps": n2,
-               "ms_per_step": round(ems / n2, 3)}
-        del hx, hy, dx
+               "ms_per_step": round(ems / n2, 3), "chunks": len(pipe.bounds),
+               "copies_declared": True}
+        del pipe, hx, hy, haux
 
-    # ---- optional final all-gather of the outputs (N > 1)
+    # ---- N > 1: the chain with the final NCCL all-gather of the outputs.  Ranks
+    # own interleaved row blocks (shard.interleaved_block), so the gather runs
+    # chunk by chunk on a second stream while the next chunk computes.
     allgather = None
     if world > 1:
-        out = chain.a
-        gathered = torch.empty((world * T, C), dtype=out.dtype, device=dev)
-        dist.all_gather_into_tensor(gathered, out)
-        torch.cuda.synchronize()
-        barrier()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(3):
-            dist.all_gather_into_tensor(gathered, out)
-        g1.record(stream)
-        torch.cuda.synchronize()
-        gms = max_over_ranks(g0.elapsed_time(g1)) / 3
-        allgather = {"ms": round(gms, 3), "bytes_per_rank": int(out.numel() * 2),
-                     "chain_plus_gather_GBps": round(world * bytes_step / ((ms / args.steps + gms) / 1e3) / 1e9, 3)}
+        from candle3d_b200 import shard
+
+        nch = args.gather_chunks
+        rc = T // nch
+        gathered = torch.empty((world * nch * rc, C), dtype=torch.bfloat16, device=dev)
+        comm = torch.cuda.Stream()
+
+        def chain_and_gather():
+            for c in range(nch):
+                chain.step(None, (c * rc, (c + 1) * rc))
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    shard.gather_chunk(gathered, chain.a[c * rc:(c + 1) * rc], c, world)
+            stream.wait_stream(comm)
+
+        def gather_only():
+            dist.all_gather_into_tensor(gathered, chain.a[:nch * rc])
+
+        def timed(fn, n):
+            fn()
+            torch.cuda.synchronize()
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            for _ in range(n):
+                fn()
+            g1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            return max_over_ranks(g0.elapsed_time(g1)) / n
+
+        gsteps = max(3, min(args.steps, 10))
+        gms = timed(gather_only, gsteps)
+        cgms = timed(chain_and_gather, gsteps)
+        per_rank = nch * rc * C * 2
+        ingress = (world - 1) * per_rank
+        v_g = world * 12.0 * nch * rc * C / (cgms / 1e3) / 1e9
+        allgather = {
+            "method": f"chain in {nch} row chunks, NCCL all_gather_into_tensor of chunk c on a "
+                      "second stream while chunk c + 1 computes (interleaved row blocks)",
+            "bytes_per_rank": per_rank, "ingress_bytes_per_rank": ingress,
+            "gather_alone_ms": round(gms, 3),
+            "gather_alone_ingress_GBps": round(ingress / (gms / 1e3) / 1e9, 1),
+            "chain_plus_gather_ms": round(cgms, 3),
+            "value_with_gather": round(v_g, 3), "unit": "GB/s",
+            "with_gather_over_value": round(v_g / value, 4),
+            "bound": "NVLink ingress: (N-1) x bytes_per_rank per step on every GPU "
+                     "(770 GB/s measured peer copy per direction)",
+            "ingress_floor_ms": round(ingress / 770e9 * 1e3, 3),
+        }
         del gathered
 
-    cpu = None
+    # ---- CPU leg (rank 0): the oracle checks the timed output's first rows,
+    # then, at N = 1, is timed as the CPU baseline.
+    cpu = parity = None
+    if rank == 0 and check_rows > 0:
+        from oracle import oracle as orc
+
+        orc.use_all_host_threads()
+        host = {k: (v[:check_rows].cpu() if k in ("x", "aux") else
+                    (v.cpu() if hasattr(v, "cpu") else tuple(p.cpu() for p in v)))
+                for k, v in inp.items()}
+        ref = chain_reference_cpu(orc, host, C)
+        err = np.abs(y_check.astype(np.float64) - ref)
+        bound = np.maximum(2e-2, np.abs(ref) * 2.0 ** -8)
+        parity = {"rows": check_rows, "max_abs": float(err.max()),
+                  "tol": "max(2e-2, 2^-8 |ref|) vs the oracle, each op rounded to bf16",
+                  "ok": bool((err <= bound).all())}
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle as orc
 
@@ -915,6 +1207,17 @@ def main():
         gbs, n, el = time_cpu_chain(orc, C, args.cpu_sample_rows, 7, min_seconds=10.0)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": orc.num_threads(), "kind": "port",
                "sample": f"{n} passes of {args.cpu_sample_rows} rows x C={C} ({el:.1f} s), C oracle"}
+
+    # ---- the other half of the metric: tokens/s of one VGGT scene split over
+    # the N GPUs; and, at N = 1, config 1 (the f32 micro-suite)
+    del chain, inp
+    torch.cuda.empty_cache()
+    config1 = None
+    if rank == 0 and world == 1 and not args.no_config1:
+        from oracle import oracle as orc
+
+        config1 = config1_record(ops, dev, None if args.no_cpu else orc)
+    stack = None if args.no_stack else vggt_scene(args, world, rank, local)
 
     if rank == 0:
         line = {
@@ -938,6 +1241,9 @@ def main():
             "e2e": e2e,
             "allgather": allgather,
             "cpu_baseline": cpu,
+            "parity": parity,
+            "block_stack": stack,
+            "config1_fp32": config1,
         }
         print(json.dumps(line))
     if world > 1:

@@ -116,6 +116,8 @@ _SIGS = {
                                  _S], C.c_int),
     "l3d_attention_workspace_size": ([C.c_int64, C.c_int64, C.c_int64, C.c_int64], C.c_size_t),
     "l3d_attention": ([_P, _P, _P, C.c_float, _P, C.c_void_p, C.c_size_t, _S], C.c_int),
+    "l3d_attention_selftest_timeout": ([_P, _P, _P, C.c_float, _P, C.c_void_p, C.c_size_t,
+                                        C.c_uint32, _S], C.c_int),
     "l3d_gguf_index": ([C.c_void_p, C.c_uint64, C.c_void_p, C.c_int64, C.POINTER(C.c_int64),
                         C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)], C.c_int),
     "l3d_gguf_metadata_string": ([C.c_void_p, C.c_uint64, C.c_char_p, C.POINTER(C.c_void_p),

@@ -105,10 +105,47 @@ class VggtAggregator:
         a = _attend(q, k, qkv[2])
         return F.linear(a.transpose(1, 2).reshape(B, N, C), p["proj_w"], p["proj_b"])
 
-    def forward(self, tokens, frame_pos, global_pos, S):
-        """tokens [B*S, N, C] -> final tokens [B*S, N, C] (residual stream updated in place)."""
+    def _attn_split(self, p, y, pos, split):
+        """Global attention of one scene whose token slabs live on the ranks of
+        `split` (shard.SceneSplit): y [1, L, C] and pos [1, L, 2] are this
+        rank's slab.  q/k are normed and rotated on the local tokens straight
+        into the head-group-major send buffer, exchanged head-parallel,
+        attended over all tokens, and the outputs sent back to their owners."""
+        _, L, C = y.shape
+        H, D, world = self.H, self.D, split.world
+        h = H // world
+        qkv = F.linear(y, p["qkv_w"], p["qkv_b"]).view(L, 3, world, h, D)
+        send = torch.empty(world, L, 3, h, D, dtype=y.dtype, device=y.device)
+        # [world, h, L, D] views: head j * h + i of the layer is head i of group j;
+        # the positions are shared by the groups (batch stride 0).
+        qin, kin = (qkv[:, i].permute(1, 2, 0, 3) for i in range(2))
+        qo, ko = (send[:, :, i].permute(0, 2, 1, 3) for i in range(2))
+        ops.qk_layernorm_rope2d(qin, kin, p["qnw"], p["qnb"], p["knw"], p["knb"], 1e-5,
+                                pos.expand(world, L, 2), 100.0, q_out=qo, k_out=ko)
+        send[:, :, 2].copy_(qkv[:, 2].transpose(0, 1))
+        q, k, v = split.exchange_qkv(send)
+        if _ATTENTION == "l3d":
+            a = torch.empty(world * L, h, D, dtype=y.dtype, device=y.device)
+            ops.attention(q, k, v, out=a.permute(1, 0, 2).unsqueeze(0))
+        else:
+            a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).contiguous()
+        o = split.return_heads(a)
+        return F.linear(o.view(1, L, C), p["proj_w"], p["proj_b"])
+
+    def forward(self, tokens, frame_pos, global_pos, S, split=None):
+        """tokens [B*S, N, C] -> final tokens [B*S, N, C] (residual stream updated in place).
+
+        With `split` (shard.SceneSplit over W ranks, B = 1) the arguments are
+        this rank's S views of a W * S-view scene (its frame positions and its
+        slab of the global positions): frame blocks run locally and global
+        blocks exchange q/k/v head-parallel across the ranks."""
         BS, N, C = tokens.shape
         B = BS // S
+        if split is not None and split.world > 1:
+            if B != 1 or self.H % split.world:
+                raise ValueError("a split scene needs B = 1 and heads divisible by the ranks")
+        else:
+            split = None
         x = tokens.contiguous()
         y = ops.layer_norm(x, self.blocks[0]["n1w"], self.blocks[0]["n1b"], 1e-5)
         nb = len(self.blocks)
@@ -116,7 +153,10 @@ class VggtAggregator:
             is_global = i % 2 == 1
             shape = (B, S * N, C) if is_global else (BS, N, C)
             xv, yv = x.view(shape), y.view(shape)
-            o = self._attn(p, yv, global_pos if is_global else frame_pos)
+            if is_global and split is not None:
+                o = self._attn_split(p, yv, global_pos, split)
+            else:
+                o = self._attn(p, yv, global_pos if is_global else frame_pos)
             _, y2 = ops.residual_layer_norm_modulate(xv, o, gate=p["ls1"], weight=p["n2w"],
                                                      bias=p["n2b"], eps=1e-5, inplace=True)
             h = ops.gelu_erf(F.linear(y2, p["fc1_w"], p["fc1_b"]))

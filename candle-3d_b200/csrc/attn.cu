@@ -90,6 +90,8 @@ struct Cfg {
   // No alignment slack: with no static shared memory the dynamic window
   // starts 1024-byte aligned (checked at run time).
   static constexpr int SMEM = NT * Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 256;
+  // The 256 bytes after the tiles: 1 + 2 STAGES + 4 NT + NMMA mbarriers, the
+  // abort flag and the TMEM address (checked below, once NMMA is known).
   static constexpr uint32_t IDESC_S = make_idesc(128, BKV);
   static constexpr uint32_t IDESC_O = make_idesc(128, D) | (1u << 16);  // B (V) MN-major
   // TMEM columns.  For D = 64, P_t has columns of its own (SEP_P), so that
@@ -105,6 +107,7 @@ struct Cfg {
   // in a fixed interleave (P_0 V, S_0, P_1 V, S_1), which measured faster.
   static constexpr int NMMA = SEP_P ? NT : 1;
   static constexpr int THREADS = (1 + NMMA + 4 * NT) * 32;  // producer, MMA, softmax
+  static_assert((1 + 2 * STAGES + 4 * NT + NMMA) * 8 + 8 <= 256, "barrier area");
   // Of every 8 pairs of P, this many take ex2_poly2 (D = 64 is bound by the
   // MUFU; at D = 128 the MUFU has room).
   static constexpr int POLY = D == 64 ? POLY_PAIRS : 0;
@@ -118,6 +121,8 @@ struct Params {
   void* out;            // [B, H, nq, D] bf16
   int64_t ob, oh, on;   // out strides (elements)
   int* status;
+  uint64_t wait_ns;     // limit of every mbarrier wait
+  int hold_kv;          // failure self-test: this key tile is never loaded (-1: none)
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -238,8 +243,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   uint64_t* p_full = s_full + NT;                      // [NT]
   uint64_t* pv_done = p_full + NT;                     // [NT] (SEP_P: every P V^T; else the last)
   uint64_t* s_free = pv_done + NT;                     // [NT] (SEP_P only)
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(s_free + NT);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + NT + 1);
+  uint64_t* mma_drain = s_free + NT;                   // [NMMA] abort teardown only
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_drain + C::NMMA);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + C::NMMA + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * (NT * BQ), h = blockIdx.y, b = blockIdx.z;
@@ -249,9 +255,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
   const int ntv = int((p.nq - q0 + BQ - 1) / BQ) < NT ? int((p.nq - q0 + BQ - 1) / BQ) : NT;
   // MMA warps with work: each commits the release of every K / V stage.
   const int nmma = C::SEP_P ? ntv : 1;
+  // Loads thread 0 issued into each ring stage: an aborting CTA waits for
+  // the last of them before it exits.
+  int nload[C::STAGES];
+#pragma unroll
+  for (int s = 0; s < C::STAGES; ++s) nload[s] = 0;
   // Key tile j (K and V, 128 keys) into ring stage j % STAGES (thread 0).
   auto load_kv = [&](int j) {
     const int s = j % C::STAGES;
+    if (j == p.hold_kv) return;  // self-test: the stage never fills
+    ++nload[s];
     mbar_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
     uint8_t* kt = sk + s * C::K_BYTES;
     for (int dc = 0; dc < C::DC; ++dc)
@@ -275,6 +288,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       mbar_init(&s_free[t], 4);
       mbar_init(&pv_done[t], 1);
     }
+    for (int w = 0; w < C::NMMA; ++w) mbar_init(&mma_drain[w], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // The Q tiles and the first key tiles start loading before the TMEM
@@ -305,7 +319,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     if (lane == 0) {
       for (int j = C::STAGES; j < nkv && !*abort_flag; ++j) {
         const int s = j % C::STAGES;
-        if (!mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, ST_TIMEOUT))
+        if (!mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns))
           break;
         load_kv(j);
       }
@@ -343,8 +357,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
           umma_f16_ts<C::IDESC_O>(tmem_base + C::COL_O + t * D, ta + uint32_t(ks * 8),
                                   db + uint64_t(ks * (16 * 128 >> 4)), (j | ks) ? 1u : 0u);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT) &&
-                mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT, p.wait_ns) &&
+                mbar_wait(&kv_full[0], 0, abort_flag, p.status, ST_TIMEOUT, p.wait_ns);
       if (ok) {
         tc_fence_after();
         for (int t = t0; t < t1; ++t) issue_s(t, 0);
@@ -355,7 +369,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         auto wait_kv = [&]() {
           if (!kv_ready)
             kv_ready = mbar_wait(&kv_full[(j + 1) % C::STAGES], ((j + 1) / C::STAGES) & 1,
-                                 abort_flag, p.status, ST_TIMEOUT);
+                                 abort_flag, p.status, ST_TIMEOUT, p.wait_ns);
           return kv_ready;
         };
         for (int t = t0; ok && t < t1; ++t) {
@@ -363,21 +377,21 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
             // S_t(j+1) as soon as the softmax warps have copied S_t(j) to
             // registers, then O_t += P_t(j) V(j)^T once P_t(j) is written.
             if (more) {
-              if (!wait_kv() || !mbar_wait(&s_free[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) {
+              if (!wait_kv() || !mbar_wait(&s_free[t], j & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
               issue_s(t, j + 1);
             }
-            if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+            if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, j);
             umma_commit(&pv_done[t]);
             if (t == t1 - 1) umma_commit(&kv_empty[j % C::STAGES]);
           } else {
             // O_t += P_t(j) V(j)^T, then S_t(j+1) over the consumed P_t(j).
-            if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+            if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, j);
             if (t == t1 - 1) umma_commit(&kv_empty[j % C::STAGES]);
@@ -406,7 +420,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     float2 l2 = f2(0.f);                         // running row sum (two halves)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) { ok = false; break; }
       tc_fence_after();
       // The row's scores into registers; S is then free for S(j + 1).
       float sv[BKV];
@@ -440,7 +454,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
       if (j > 0) {
         if (__any_sync(0xffffffffu, grow)) {
           if (!pv_waited) {
-            if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+            if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) { ok = false; break; }
             tc_fence_after();
             pv_waited = true;
           }
@@ -473,7 +487,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
         u[e >> 1] = pack_bf16x2(f.x, f.y);
       }
       if (!pv_waited) {  // P_t(j-1) V^T has read P_t
-        if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT)) { ok = false; break; }
+        if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
       }
 #pragma unroll
@@ -487,7 +501,7 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     }
     // Epilogue: O / l, bf16, after the last P V^T.
     if (ok && nkv > 0 &&
-        mbar_wait_idle(&pv_done[t], C::SEP_P ? (nkv - 1) & 1 : 0, abort_flag, p.status, ST_TIMEOUT)) {
+        mbar_wait_idle(&pv_done[t], C::SEP_P ? (nkv - 1) & 1 : 0, abort_flag, p.status, ST_TIMEOUT, p.wait_ns)) {
       tc_fence_after();
       const float l = l2.x + l2.y;
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -511,12 +525,24 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1)
     }
   }
 
-  // Teardown: MMAs complete before TMEM is released (bounded).
+  // Teardown.  After an abort nothing the CTA started may still be running
+  // when it frees TMEM and exits: each MMA-issuing thread commits its issued
+  // MMAs to a drain barrier and waits for it, and thread 0 waits for the last
+  // TMA load it issued into the Q tiles and into each K / V stage (all
+  // bounded).  The normal path needs neither: every MMA was waited for
+  // through pv_done and every load consumed.
   tc_fence_before();
   __syncthreads();
-  if (*abort_flag && threadIdx.x == 32) {
-    const uint64_t t1 = globaltimer();
-    while (globaltimer() - t1 < 1000000ull) {
+  if (*abort_flag) {
+    if (warp >= 1 && warp <= C::NMMA && lane == 0) {
+      umma_commit(&mma_drain[warp - 1]);
+      mbar_drain(&mma_drain[warp - 1], 0, p.wait_ns);
+    }
+    if (threadIdx.x == 0) {
+      if (ntv > 0) mbar_drain(q_full, 0, p.wait_ns);
+#pragma unroll
+      for (int s = 0; s < C::STAGES; ++s)
+        if (nload[s] > 0) mbar_drain(&kv_full[s], uint32_t(nload[s] - 1) & 1u, p.wait_ns);
     }
   }
   __syncthreads();
@@ -562,10 +588,10 @@ extern "C" size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk,
   return 256;  // the status word; q, k and v are read in place
 }
 
-extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v,
-                             float scale, const l3d_tensor* out, void* workspace,
-                             size_t workspace_bytes, l3d_stream stream) {
-  const char* op = "l3d_attention";
+static int run_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v,
+                         float scale, const l3d_tensor* out, void* workspace,
+                         size_t workspace_bytes, l3d_stream stream, uint64_t wait_ns, int hold_kv,
+                         const char* op) {
   using namespace l3d::attn;
   const l3d_tensor* all[] = {q, k, v, out};
   for (const l3d_tensor* t : all) {
@@ -636,18 +662,35 @@ extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d
   p.oh = out->strides[1];
   p.on = out->strides[2];
   p.status = status;
+  p.wait_ns = wait_ns;
+  p.hold_kv = hold_kv;
   const dim3 grid(unsigned((nq + NT * BQ - 1) / (NT * BQ)), unsigned(H), unsigned(B));
-  static std::once_flag once;
-  static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                Cfg<64>::SMEM);
-    if (attr == cudaSuccess)
-      attr = cudaFuncSetAttribute(attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Cfg<128>::SMEM);
-  });
+  const cudaError_t attr =
+      D == 64 ? set_smem_limit(reinterpret_cast<const void*>(attn_kernel<64>), Cfg<64>::SMEM)
+              : set_smem_limit(reinterpret_cast<const void*>(attn_kernel<128>), Cfg<128>::SMEM);
   if (attr != cudaSuccess) return fail(L3D_E_CUDA, "%s: cannot reserve shared memory", op);
   if (D == 64) attn_kernel<64><<<grid, Cfg<64>::THREADS, Cfg<64>::SMEM, s>>>(map_q, map_k, map_v, p);
   else attn_kernel<128><<<grid, Cfg<128>::THREADS, Cfg<128>::SMEM, s>>>(map_q, map_k, map_v, p);
   return check_launch(op);
+}
+
+extern "C" int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v,
+                             float scale, const l3d_tensor* out, void* workspace,
+                             size_t workspace_bytes, l3d_stream stream) {
+  return run_attention(q, k, v, scale, out, workspace, workspace_bytes, stream,
+                       l3d::tc::WAIT_LIMIT_NS, -1, "l3d_attention");
+}
+
+extern "C" int l3d_attention_selftest_timeout(const l3d_tensor* q, const l3d_tensor* k,
+                                              const l3d_tensor* v, float scale,
+                                              const l3d_tensor* out, void* workspace,
+                                              size_t workspace_bytes, uint32_t wait_limit_ms,
+                                              l3d_stream stream) {
+  const char* op = "l3d_attention_selftest_timeout";
+  if (wait_limit_ms == 0 || wait_limit_ms > 2000)
+    return fail(L3D_E_UNSUPPORTED, "%s: wait_limit_ms must be in [1, 2000]", op);
+  if (k && k->ndim == 4 && k->dims[2] == 0)
+    return fail(L3D_E_UNSUPPORTED, "%s: needs at least one key", op);
+  return run_attention(q, k, v, scale, out, workspace, workspace_bytes, stream,
+                       uint64_t(wait_limit_ms) * 1000000ull, 0, op);
 }

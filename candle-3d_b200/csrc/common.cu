@@ -3,7 +3,9 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
@@ -53,6 +55,21 @@ int sm_count() {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+cudaError_t set_smem_limit(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, cudaError_t> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_pair(dev, kernel);
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  done[key] = e;
+  return e;
 }
 
 bool make_rowmap(const l3d_tensor* t, int lead, RowMap* m) {

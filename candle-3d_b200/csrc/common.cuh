@@ -34,6 +34,11 @@ const char* dtype_name(int dt);
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (device, kernel): the attribute belongs to the device
+// context, so a process that drives several GPUs sets it on each.  Returns
+// the result of the first attempt on this device.
+cudaError_t set_smem_limit(const void* kernel, int bytes);
 
 // Byte address of the first element of a view.
 inline const char* elem_ptr(const l3d_tensor* t) {

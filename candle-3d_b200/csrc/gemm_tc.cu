@@ -1120,25 +1120,18 @@ static int run_dequant_linear(const l3d_tensor* x, const void* wq, int fmt, int6
                           uint64_t(res_ld)))
                   ? 1
                   : 0;
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_RAW_TMA>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ModeCfg<MODE_RAW_TMA>::SMEM);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_RAW_LDG>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      ModeCfg<MODE_RAW_LDG>::SMEM);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_BF16>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      ModeCfg<MODE_BF16>::SMEM);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_BF16_EPI8>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      ModeCfg<MODE_BF16_EPI8>::SMEM);
-  });
+  cudaError_t attr_err =
+      set_smem_limit(reinterpret_cast<const void*>(qgemm_kernel<MODE_RAW_TMA>),
+                     ModeCfg<MODE_RAW_TMA>::SMEM);
+  if (attr_err == cudaSuccess)
+    attr_err = set_smem_limit(reinterpret_cast<const void*>(qgemm_kernel<MODE_RAW_LDG>),
+                              ModeCfg<MODE_RAW_LDG>::SMEM);
+  if (attr_err == cudaSuccess)
+    attr_err = set_smem_limit(reinterpret_cast<const void*>(qgemm_kernel<MODE_BF16>),
+                              ModeCfg<MODE_BF16>::SMEM);
+  if (attr_err == cudaSuccess)
+    attr_err = set_smem_limit(reinterpret_cast<const void*>(qgemm_kernel<MODE_BF16_EPI8>),
+                              ModeCfg<MODE_BF16_EPI8>::SMEM);
   if (attr_err != cudaSuccess)
     return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
   const int tiles = int(((M + BM - 1) / BM) * ((n + BN - 1) / BN));
@@ -1279,13 +1272,8 @@ extern "C" int l3d_sparse_conv3d(const l3d_tensor* feats, const l3d_tensor* nbr,
                     ? 1
                     : 0;
   if (!p.tma_store) map_y = map_w;  // unused
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_GATHER>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ModeCfg<MODE_GATHER>::SMEM);
-  });
+  const cudaError_t attr_err = set_smem_limit(
+      reinterpret_cast<const void*>(qgemm_kernel<MODE_GATHER>), ModeCfg<MODE_GATHER>::SMEM);
   if (attr_err != cudaSuccess)
     return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
   const int tiles = int(((n + BM - 1) / BM) * ((cout + BN - 1) / BN));
@@ -1538,13 +1526,8 @@ extern "C" int l3d_sparse_conv3d_pairs(const l3d_tensor* feats, const l3d_tensor
       return fail(L3D_E_CUDA, "%s: cuTensorMapEncodeTiled failed for the weights", op);
     p.tma_store = make_map_y(&map_y, prod, L3D_F32, uint64_t(L.rows), uint64_t(cout), uint64_t(L.ld)) ? 1 : 0;
     if (!p.tma_store) map_y = map_w;  // unused
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-      attr_err = cudaFuncSetAttribute(qgemm_kernel<MODE_PAIRS>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      ModeCfg<MODE_PAIRS>::SMEM);
-    });
+    const cudaError_t attr_err = set_smem_limit(
+        reinterpret_cast<const void*>(qgemm_kernel<MODE_PAIRS>), ModeCfg<MODE_PAIRS>::SMEM);
     if (attr_err != cudaSuccess)
       return fail(L3D_E_CUDA, "%s: cannot reserve the kernel's shared memory", op);
     const int tiles = int((L.rows / BM) * ((cout + BN - 1) / BN));

@@ -31,12 +31,21 @@ __device__ __forceinline__ float inv_freq_f32(float theta, float num, float den)
 }
 
 // sin / cos of an exactly formed angle: the accurate libm form for f32
-// activations; the hardware approximation for 16-bit activations (absolute
-// error about 1e-5 at |angle| <= 64, far below half an ulp of bf16 / f16).
+// activations; for 16-bit activations the hardware approximation after a
+// Cody-Waite reduction by 2*pi (two-constant split: the f32 value of 2*pi and
+// its f32 rounding error), so the error stays at the [-pi, pi] level (a few
+// 1e-7) for any coordinate: TRELLIS.2 voxel coordinates reach 1023 and the
+// unreduced hardware form loses accuracy in proportion to |angle|.
 template <typename T>
 __device__ __forceinline__ void sincos_t(float a, float* s, float* c) {
-  if constexpr (sizeof(T) == 2) __sincosf(a, s, c);
-  else sincosf(a, s, c);
+  if constexpr (sizeof(T) == 2) {
+    const float k = rintf(a * 0.159154943091895336f);  // a / (2 pi), nearest
+    float r = fmaf(-k, 6.28318548202514648f, a);        // f32(2 pi) = 2 pi + 1.7484555e-7
+    r = fmaf(k, 1.74845553e-7f, r);
+    __sincosf(r, s, c);
+  } else {
+    sincosf(a, s, c);
+  }
 }
 
 __device__ __forceinline__ float load_index_f(const void* p, int dtype, int64_t off) {

@@ -227,15 +227,15 @@ __global__ void index_select_kernel(const T* __restrict__ feats, int64_t fs0, in
   }
 }
 
-static uint64_t table_cap(int64_t n) {
+static constexpr uint64_t table_cap(int64_t n) {
   uint64_t cap = 64;
   while (cap < uint64_t(2 * n)) cap <<= 1;
   return cap;
 }
 
-static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+static constexpr size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-static size_t sparse_ws_bytes(int64_t n) {
+static constexpr size_t sparse_ws_bytes(int64_t n) {
   const uint64_t cap = table_cap(n);
   const int64_t tiles = (n + kTile - 1) / kTile;
   return align256(cap * 8) + align256(cap * 4) + align256(size_t(27) * (tiles > 0 ? tiles : 1) * 4);
@@ -369,6 +369,12 @@ constexpr size_t kNoAllocTiles = (kNoAllocMaxCoords + kTile - 1) / kTile;
 constexpr size_t kNoAllocBytes = ((kNoAllocCap * 8 + 255) & ~size_t(255)) +
                                  ((kNoAllocCap * 4 + 255) & ~size_t(255)) +
                                  ((27 * kNoAllocTiles * 4 + 255) & ~size_t(255));
+// The fixed array must hold the workspace layout of the largest input.
+static_assert(kNoAllocCap >= 2 * kNoAllocMaxCoords, "table needs two slots per coordinate");
+static_assert((kNoAllocCap & (kNoAllocCap - 1)) == 0, "table size is a power of two");
+static_assert(table_cap(kNoAllocMaxCoords) <= kNoAllocCap, "table of the largest input fits");
+static_assert(kNoAllocBytes == sparse_ws_bytes(kNoAllocMaxCoords),
+              "scratch bytes equal the workspace layout of the largest input");
 static __device__ __align__(256) unsigned char g_pairs_scratch[kNoAllocBytes];
 
 // Device address of g_pairs_scratch on the current device.  The host-side name
@@ -437,6 +443,9 @@ extern "C" int l3d_sparse_neighbor_pairs_noalloc(const l3d_tensor* coords,
   SparseWs ws;
   ws.cap = table_cap(n);
   ws.tiles = (n + kTile - 1) / kTile;
+  if (sparse_ws_bytes(n) > kNoAllocBytes || ws.cap > kNoAllocCap)
+    return fail(L3D_E_UNSUPPORTED, "%s: scratch layout of %lld coordinates exceeds the array", op,
+                (long long)n);
   char* base = static_cast<char*>(scratch);
   ws.keys = reinterpret_cast<unsigned long long*>(base);
   base += align256(ws.cap * 8);

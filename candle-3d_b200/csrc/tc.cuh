@@ -63,11 +63,12 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
 }
 // Bounded wait for the warps that are not on the MMA critical path.
 __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity,
-                                               volatile int* abort_flag, int* status, int code) {
+                                               volatile int* abort_flag, int* status, int code,
+                                               uint64_t limit_ns = WAIT_LIMIT_NS) {
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait_suspend(bar, parity)) {
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(status, 0, code);
       return false;
@@ -78,19 +79,30 @@ __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity,
 // Bounded wait: returns false (and raises the CTA abort flag) on timeout or
 // when another role of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+                                          int* status, int code,
+                                          uint64_t limit_ns = WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(status, 0, code);
       return false;
     }
   }
+}
+// Teardown after an abort: waits (bounded, ignoring the abort flag) for a
+// phase the CTA itself started (a TMA load it issued, a commit of its MMAs),
+// so that no copy into shared memory or tensor-core operation is still in
+// flight when the CTA frees its tensor memory and exits.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait_suspend(bar, parity))
+    if (globaltimer() - t0 > limit_ns) return false;
+  return true;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,

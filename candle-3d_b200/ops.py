@@ -9,6 +9,8 @@ Invalid inputs raise `L3dError` carrying the library's status and message.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
@@ -455,14 +457,28 @@ class SparseConv3d:
         return out
 
 
+# Status-word workspaces of l3d_attention, one per (device, stream): calls on
+# different streams then never clear or overwrite each other's status.
 _ATTN_WS = {}
+# Read the status word back after every attention call (synchronises the
+# stream) and raise on a kernel-reported error; also on with L3D_CHECK_STATUS=1.
+CHECK_STATUS = os.environ.get("L3D_CHECK_STATUS", "0") == "1"
 
 
-def attention(q, k, v, scale=None, out=None):
+def attention_workspace(device, stream=None):
+    """The status-word workspace ops.attention uses on (device, stream)."""
+    st = torch.cuda.current_stream(device) if stream is None else stream
+    return _ATTN_WS.get((torch.device(device), st.cuda_stream))
+
+
+def attention(q, k, v, scale=None, out=None, check=None):
     """exact_sdpa_heads (crate/runtime/attention_math.rs:199-259): softmax(q k^T
     * scale) v on [B, H, N, D] bf16 views (D = 64 or 128), tcgen05 flash
     attention.  `out` defaults to token-major [B, N, H, D] memory viewed as
-    [B, H, N, D], so out.transpose(1, 2).reshape(B, N, H * D) is a view."""
+    [B, H, N, D], so out.transpose(1, 2).reshape(B, N, H * D) is a view.
+    With `check` (default CHECK_STATUS) the stream is synchronised and a
+    non-zero status word (a bounded wait in the kernel ran out) raises
+    L3dError(L3D_E_DEVICE)."""
     _check_cuda(q, k, v, out)
     B, H, N, D = q.shape
     if scale is None:
@@ -470,10 +486,17 @@ def attention(q, k, v, scale=None, out=None):
     if out is None:
         out = torch.empty((B, N, H, D), dtype=q.dtype, device=q.device).transpose(1, 2)
     need = _lib.lib().l3d_attention_workspace_size(B, H, k.shape[2], D)
-    ws = _ATTN_WS.get(q.device)
+    stream = torch.cuda.current_stream(q.device)
+    key = (q.device, stream.cuda_stream)
+    ws = _ATTN_WS.get(key)
     if ws is None or ws.numel() < need:
         ws = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
-        _ATTN_WS[q.device] = ws
+        _ATTN_WS[key] = ws
     call("l3d_attention", ref(desc(q)), ref(desc(k)), ref(desc(v)), float(scale), ref(desc(out)),
-         ws.data_ptr(), ws.numel(), _s(q))
+         ws.data_ptr(), ws.numel(), stream.cuda_stream)
+    if CHECK_STATUS if check is None else check:
+        stream.synchronize()
+        st = int(ws[:4].view(torch.int32).item())
+        if st != 0:
+            raise _lib.L3dError(8, "l3d_attention", f"kernel status word {st} (bounded wait expired)")
     return out

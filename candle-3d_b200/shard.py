@@ -34,3 +34,74 @@ def gather_rows(local: torch.Tensor, n: int, world: int, group=None) -> torch.Te
     parts = [out[r * cap: r * cap + (shard_range(n, world, r)[1] - shard_range(n, world, r)[0])]
              for r in range(world)]
     return torch.cat(parts, 0)
+
+
+# ------------------------------------------------------ interleaved row blocks
+def interleaved_block(chunk: int, world: int, rank: int, rows_per_chunk: int) -> tuple[int, int]:
+    """Global [start, end) of rank's `chunk`-th block when ranks own row blocks
+    round-robin: block c of rank r is global rows (c * world + r) * rows_per_chunk
+    onward.  With this ownership the all-gather of every rank's chunk c fills
+    one contiguous range of the global row order, so the final gather can run
+    chunk by chunk, overlapped with the computation of the next chunk."""
+    start = (chunk * world + rank) * rows_per_chunk
+    return start, start + rows_per_chunk
+
+
+def gather_chunk(out: torch.Tensor, local_chunk: torch.Tensor, chunk: int, world: int,
+                 group=None) -> None:
+    """All-gather every rank's block `chunk` ([rows_per_chunk, ...], contiguous)
+    into its place in the global [world * chunks * rows_per_chunk, ...] output."""
+    rc = local_chunk.shape[0]
+    dist.all_gather_into_tensor(out[chunk * world * rc:(chunk + 1) * world * rc], local_chunk,
+                                group=group)
+
+
+# --------------------------------------------------- one scene across ranks
+class SceneSplit:
+    """One scene's tokens split across the ranks of a process group, for the
+    attention layers that mix all tokens (VGGT global blocks,
+    crate/runtime/vggt.rs:299-311).  Rank r owns a contiguous slab of the
+    scene's token sequence (whole views: frame blocks need no communication).
+    A global attention is computed head-parallel: each rank sends the q, k, v
+    of its tokens for head group j (H / world heads) to rank j, attends over
+    all tokens for its own head group, and sends each token slab's outputs back
+    to its owner (two all-to-alls, about (3 + 1) / world of the layer's q/k/v/o
+    bytes crossing NVLink per rank, instead of an all-gather of every rank's K
+    and V)."""
+
+    def __init__(self, group=None, world: int | None = None, rank: int | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if world is None else world
+        self.rank = dist.get_rank(group) if rank is None else rank
+
+    def all_to_all(self, send: torch.Tensor) -> torch.Tensor:
+        """Block j of dim 0 goes to rank j; block j of the result came from rank j."""
+        if self.world == 1:
+            return send
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send.contiguous(), group=self.group)
+        return recv
+
+    def exchange_qkv(self, send: torch.Tensor):
+        """send [world, L, 3, h, D]: this rank's L tokens, head group j at [j].
+        Returns q, k, v as [1, h, world * L, D] views over all tokens of this
+        rank's head group (token order = rank order = the scene's order)."""
+        world, L, three, h, D = send.shape
+        r = self.all_to_all(send).view(world * L, 3, h, D)
+        return tuple(r[:, i].permute(1, 0, 2).unsqueeze(0) for i in range(3))
+
+    def return_heads(self, out_tokens: torch.Tensor) -> torch.Tensor:
+        """out_tokens [world * L, h, D] (this head group's output, token-major)
+        -> [L, world * h * D] rows of this rank's tokens, channel = head * D + d."""
+        Lall, h, D = out_tokens.shape
+        L = Lall // self.world
+        r = self.all_to_all(out_tokens).view(self.world, L, h, D)
+        return r.permute(1, 0, 2, 3).reshape(L, self.world * h * D)
+
+    def all_gather_rows(self, local: torch.Tensor) -> torch.Tensor:
+        """[L, ...] slabs of every rank -> [world * L, ...] in rank order."""
+        if self.world == 1:
+            return local
+        out = local.new_empty((self.world * local.shape[0],) + tuple(local.shape[1:]))
+        dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
+        return out

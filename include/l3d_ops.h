@@ -22,8 +22,10 @@
  *    status (0 = ok).  On failure `l3d_last_error()` returns a thread-local
  *    message.  No entry synchronises the host; all work is enqueued on
  *    `stream`.  Entries are stateless and reentrant unless noted.
- *  - Scratch memory is always caller-provided (`workspace` + size queried
- *    with the matching `*_workspace_size` function).
+ *  - Scratch memory is caller-provided (`workspace` + size queried with the
+ *    matching `*_workspace_size` function), with one exception:
+ *    `l3d_sparse_neighbor_pairs_noalloc` keeps its scratch in a fixed
+ *    in-library device array, for callers that cannot allocate.
  */
 #ifndef L3D_OPS_H
 #define L3D_OPS_H
@@ -385,6 +387,18 @@ size_t l3d_attention_workspace_size(int64_t b, int64_t h, int64_t nk, int64_t d)
 int l3d_attention(const l3d_tensor* q, const l3d_tensor* k, const l3d_tensor* v, float scale,
                   const l3d_tensor* out, void* workspace, size_t workspace_bytes,
                   l3d_stream stream);
+
+/* Failure-handling self-test of l3d_attention (no counterpart in the
+ * reference): the same launch, except that the first key tile is never
+ * loaded and every bounded wait gives up after wait_limit_ms (1 .. 2000).
+ * The kernel must then record status 5 (timeout) in the workspace, wait for
+ * the copies and tensor-core operations it started, free its tensor memory
+ * and return, leaving the context usable; the caller reads the status word
+ * after synchronising.  Needs at least one key. */
+int l3d_attention_selftest_timeout(const l3d_tensor* q, const l3d_tensor* k,
+                                   const l3d_tensor* v, float scale, const l3d_tensor* out,
+                                   void* workspace, size_t workspace_bytes,
+                                   uint32_t wait_limit_ms, l3d_stream stream);
 
 /* ---- GGUF tensor index (the on-disk format feeding a13) ------------------------ */
 

@@ -43,7 +43,7 @@ def test_attention_matches_torch(ops, dev, B, H, N, NK, D, layout):
     scale = D ** -0.5
     out = ops.attention(q, k, v, scale)
     torch.cuda.synchronize()
-    ws = ops._ATTN_WS[q.device]
+    ws = ops.attention_workspace(q.device)
     assert ws[:4].view(torch.int32).item() == 0  # no bounded wait expired
     ref = _ref(q, k, v, scale)
     got = out.float()
@@ -88,7 +88,7 @@ def test_attention_rising_scores(ops, dev, D, span):
     q, k, v = (t.to(dev, torch.bfloat16) for t in (q, k, v))
     out = ops.attention(q, k, v, D ** -0.5)
     torch.cuda.synchronize()
-    assert ops._ATTN_WS[q.device][:4].view(torch.int32).item() == 0
+    assert ops.attention_workspace(q.device)[:4].view(torch.int32).item() == 0
     ref = _ref(q, k, v, D ** -0.5)
     err = (out.float() - ref).abs()
     assert torch.all(err <= 2e-2 * torch.clamp(ref.abs(), min=1.0)), f"max err {err.max().item():.3e}"
@@ -147,3 +147,40 @@ def test_attention_one_query_odd_heads_strided_out(ops, dev, D):
     ref = _ref(q, k, v, D ** -0.5)
     err = (out.float() - ref).abs()
     assert torch.all(err <= 2e-2 * torch.clamp(ref.abs(), min=1.0)), f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_bounded_wait_runs_out(pkg, ops, dev, D):
+    """Failure handling without a GPU fault: the self-test launch never loads
+    the first key tile, so the kernel's waits (limited to 50 ms) run out.  It
+    must record status 5 in its workspace, wait for what it started, free its
+    tensor memory and return; the context stays usable, so a normal (checked)
+    call afterwards is exact again."""
+    import ctypes as C
+
+    import torch
+
+    from candle3d_b200._lib import desc, ref
+
+    g = torch.Generator().manual_seed(5 + D)
+    q, k, v = (torch.randn(1, 2, 256, D, generator=g).to(dev, torch.bfloat16) for _ in range(3))
+    k2, v2 = (torch.randn(1, 2, 640, D, generator=g).to(dev, torch.bfloat16) for _ in range(2))
+    out = torch.zeros_like(q)
+    ws = torch.full((256,), 0xFF, dtype=torch.uint8, device=dev)
+    lib = pkg._lib.lib()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for kk, vv in ((k, v), (k2, v2)):
+        rc = lib.l3d_attention_selftest_timeout(ref(desc(q)), ref(desc(kk)), ref(desc(vv)),
+                                                C.c_float(D ** -0.5), ref(desc(out)),
+                                                C.c_void_p(ws.data_ptr()), C.c_size_t(256),
+                                                C.c_uint32(50), C.c_void_p(stream))
+        assert rc == 0, lib.l3d_last_error()
+        torch.cuda.synchronize()
+        assert ws[:4].view(torch.int32).item() == 5
+    assert lib.l3d_attention_selftest_timeout(ref(desc(q)), ref(desc(k)), ref(desc(v)),
+                                              C.c_float(1.0), ref(desc(out)),
+                                              C.c_void_p(ws.data_ptr()), C.c_size_t(256),
+                                              C.c_uint32(0), C.c_void_p(stream)) == 4
+    got = ops.attention(q, k2, v2, D ** -0.5, check=True)
+    ref_ = _ref(q, k2, v2, D ** -0.5)
+    assert (got.float() - ref_).abs().max().item() < 2e-2

@@ -44,10 +44,13 @@ def test_noalloc_matches_workspace_entry_twice(pkg, ops, dev):
 
     # First call: the TRELLIS-sized grid (~31.5k voxels); second call: a
     # smaller, unsorted set with duplicates, after the first has filled the
-    # scratch table.
+    # scratch table; third: exactly the 65536-coordinate limit (the dense
+    # 16 x 64 x 64 block, every table slot pair in use).
     first = _coords(20261201, 64, 0.12)
     second = np.random.default_rng(7).integers(0, 12, size=(900, 3)).astype(np.int32)
-    for c in (first, second):
+    third = np.argwhere(np.ones((16, 64, 64), bool)).astype(np.int32)
+    assert third.shape[0] == 65536
+    for c in (first, second, third):
         ct = torch.from_numpy(c).to(dev)
         d0, s0, n0 = ops.sparse_neighbor_pairs(ct)
         d1, s1, n1 = _noalloc_pairs(pkg, ct)

@@ -13,7 +13,7 @@ add is fused with the norm that follows it:
     GELU-erf -> fc2 -> LayerScale residual + next block's norm1 (one kernel).
   * TripoSG DiT (crate/runtime/triposg_dit.rs:217-276,346-506): sin-first
     timestep token, UViT long skips, RMSNorm-heads on the diffusers q/k/v
-    split, f32 cross attention, exact-GELU FFN.
+    split, bf16 flash cross attention, exact-GELU FFN.
   * TRELLIS.2 SLAT (crate/runtime/trellis2_blocks.rs:609-646,
     crate/runtime/trellis2_dit.rs:549-574): shared adaLN, modulated norms,
     L2-norm * gamma + 3D RoPE on integer voxel coordinates, Q8_0 weights through
@@ -268,8 +268,9 @@ class TripoSgDit:
         kv = F.linear(cond, p["kv2_w"]).view(B, cond.shape[1], H, 2 * D)
         k = ops.rms_norm_heads(kv[..., :D].transpose(1, 2), p["nk2"], 1e-6)
         v = kv[..., D:].transpose(1, 2)
-        # exact_sdpa_heads runs in f32 (crate/runtime/attention_math.rs:244-259).
-        a = F.scaled_dot_product_attention(q.float(), k.float(), v.float()).to(y.dtype)
+        # bf16 operands with f32 softmax / accumulation inside the flash kernel,
+        # as for the self attention (the stack parity tests bound the result).
+        a = _attend(q, k, v)
         return F.linear(a.transpose(1, 2).reshape(B, L, C), p["o2_w"], p["o2_b"])
 
     def timestep_token(self, t, B):

@@ -92,7 +92,10 @@ def test_qk_layernorm_rope2d_bench_grid(ops, orc, dev, dt):
 @pytest.mark.parametrize("C", [1024, 1536, 2048])
 def test_bench_chain_matches_oracle(ops, orc, dev, C):
     """bench.py's timed Chain (the kernels and buffers it launches) on 8192
-    rows of its own seeded inputs, against its CPU restatement."""
+    rows of its own seeded inputs: each kernel against the oracle's op on the
+    same input (the bench's own parity record), and the chain end to end
+    against the oracle's chain within two bf16 ulps (one op's output may round
+    to the other neighbour, which the next op carries on)."""
     import bench
 
     T = 8192
@@ -100,6 +103,13 @@ def test_bench_chain_matches_oracle(ops, orc, dev, C):
     inp = {k: (v.to(dev) if hasattr(v, "to") else tuple(p.to(dev) for p in v))
            for k, v in host.items()}
     chain = bench.Chain(ops, inp, T, C)
-    y = chain.step().float().cpu().numpy()
+    stages = chain.stage_outputs(T)
+    prev = None
+    for i, got in enumerate(stages):
+        assert_close(got, bench.chain_stage_reference(orc, host, C, i, prev), "bf16",
+                     f"bench chain C={C} op {i}")
+        prev = got
+    assert bench.chain_parity(orc, host, C, stages)["ok"]
     ref = bench.chain_reference_cpu(orc, host, C)
-    assert_close(y, ref, "bf16", f"bench chain C={C}")
+    err = np.abs(stages[2] - ref)
+    assert (err <= np.maximum(2e-2, np.abs(ref) * 2.0 ** -6)).all(), float(err.max())

@@ -549,7 +549,7 @@ def vggt_scene(args, world, rank, local, check=True):
         return step
 
     step = runner((v0, v0 + sl), split)
-    px = inp["pixels"][v0:v0 + sl].contiguous()
+    px = inp["pixels"][v0:v0 + sl].clone()
     stream = torch.cuda.current_stream(dev)
 
     def barrier():

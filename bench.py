@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-stack", action="store_true",
                     help="chain workload: skip the VGGT one-scene block_stack sub-record")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="VGGT stack: launch the step's kernels one by one, not as a CUDA graph")
     ap.add_argument("--no-config1", action="store_true",
                     help="chain workload: skip the config-1 f32 micro-suite sub-record")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
@@ -569,10 +571,25 @@ def vggt_scene(args, world, rank, local, check=True):
     for _ in range(max(args.warmup, 3)):
         out = step(px)
     barrier()
+    # The step (about 250 kernels and, split, 48 all-to-alls) is captured once
+    # as a CUDA graph and replayed: at 1 / N of a scene per GPU, the host-side
+    # launch of each op would otherwise take longer than the op.
+    graph = None
+    run = lambda: step(px)  # noqa: E731
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out_g = step(px)
+        graph.replay()
+        barrier()
+        run = lambda: (graph.replay(), out_g)[1]  # noqa: E731
+        for _ in range(2):
+            run()
+        barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        out = step(px)
+        out = run()
     e1.record(stream)
     barrier()
     ms = maxr(e0.elapsed_time(e1)) / args.steps
@@ -586,14 +603,13 @@ def vggt_scene(args, world, rank, local, check=True):
     # End to end: this rank's views' pixels in from pinned host memory, the
     # gathered scene tokens back out, every step.
     hp = px.cpu().pin_memory()
-    dp = torch.empty_like(px)
     hy = torch.empty((tokens, C), dtype=torch.bfloat16).pin_memory()
     barrier()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
     for _ in range(args.steps):
-        dp.copy_(hp, non_blocking=True)
-        hy.copy_(step(dp), non_blocking=True)
+        px.copy_(hp, non_blocking=True)  # the step's (graph's) input buffer
+        hy.copy_(run(), non_blocking=True)
     a1.record(stream)
     barrier()
     ems = maxr(a0.elapsed_time(a1)) / args.steps
@@ -605,7 +621,7 @@ def vggt_scene(args, world, rank, local, check=True):
         "parallelism": (f"scene split over {world} GPUs: {sl} view(s) per rank, global blocks "
                         f"head-parallel ({16 // world} heads per rank, 2 NCCL all-to-alls)")
                        if world > 1 else "single GPU",
-        "attention": args.attention,
+        "attention": args.attention, "cuda_graph": graph is not None,
         "roofline": {"bound": "tensor", "achieved_per_gpu": round(ach, 1), "peak": peak_tf,
                      "unit": "TFLOP/s", "frac": round(ach / peak_tf, 4),
                      "flops_per_scene": float(flops)},
@@ -623,6 +639,9 @@ def vggt_scene(args, world, rank, local, check=True):
             rec["parity_vs_single_gpu"] = {"rel_l2": rel, "max_abs": float(d.abs().max()),
                                            "tol": "rel L2 < 2e-2 (bf16 stack)", "ok": rel < 2e-2}
         barrier()
+    # A graph that holds NCCL calls is released before the process group goes.
+    del graph, run
+    torch.cuda.synchronize()
     return rec
 
 

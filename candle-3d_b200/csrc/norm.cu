@@ -9,6 +9,7 @@
 // read from HBM once and written once, with the reductions done by warp
 // shuffles (G <= 32) or shuffles plus one shared-memory exchange (G > 32).
 #include "common.cuh"
+#include "ring.cuh"
 
 namespace l3d {
 
@@ -403,6 +404,202 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
   }
 }
 
+// ------------------------------------------------------------ ring variant
+// Rows without a residual branch, long enough inputs: one CTA per SM streams
+// its contiguous block of rows through a ring of shared-memory slots filled by
+// bulk copies (cp.async.bulk, one per row, issued by eight producer lanes of
+// warp 0, so up to `nslot` rows are in flight per SM without holding them in
+// registers); consumer warps each take every NW-th row: copy it from its
+// slot into registers, release the slot, reduce with shuffles and store the
+// normalised, modulated row directly.  The arithmetic and its order are
+// those of the register kernel above (G = 32, folded coefficients), so both
+// give identical bits.  Every mbarrier wait is bounded; on expiry the block
+// records status 5 in g_norm_status, waits (bounded) for the copies it
+// issued and returns.
+constexpr int kRingProducers = 8;
+constexpr int kRingMaxSlots = 96;
+constexpr size_t kRingSmem = 200 * 1024;  // coefficients + slots + barriers
+__device__ int g_norm_status;
+
+struct RingCfg {
+  int nslot;             // multiple of kRingProducers
+  uint32_t row_bytes;    // C * element size (a multiple of 16)
+  size_t coef_bytes;     // 128-aligned
+  uint64_t wait_ns;
+};
+
+template <typename T, int NV, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 1)
+    rowring_kernel(const RowNormParams p, const RingCfg rc) {
+  constexpr int VEC = 16 / int(sizeof(T));
+  constexpr int P = VEC / 2;
+  extern __shared__ __align__(128) unsigned char ring_smem[];
+  const int64_t C = p.C;
+  const int64_t nc = int64_t(p.nbatch) * C;
+  float* coef = reinterpret_cast<float*>(ring_smem);  // A [nc], Bc [nc] (, gate [nc])
+  unsigned char* slots = ring_smem + rc.coef_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + size_t(rc.nslot) * rc.row_bytes);
+  uint64_t* empty = full + rc.nslot;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + rc.nslot);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < rc.nslot; ++s) {
+      ring_bar_init(&full[s], 1);
+      ring_bar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    ring_init_fence();
+  }
+  __syncthreads();
+  const int64_t per = (p.rows + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = int64_t(blockIdx.x) * per;
+  const int64_t n = r0 < p.rows ? (p.rows - r0 < per ? p.rows - r0 : per) : 0;
+  // Producer lane L issues rows L, L + 8, ...; row k lives in slot k % nslot,
+  // so lane L alone fills the slots s = L (mod 8).
+  int64_t last = -1;  // the last row this producer lane issued
+  auto issue = [&](int64_t k) {
+    const int s = int(k % rc.nslot);
+    const T* src = static_cast<const T*>(p.x) + row_offset(p.xm, r0 + k);
+    ring_load(slots + size_t(s) * rc.row_bytes, src, rc.row_bytes, &full[s]);
+    last = k;
+  };
+  const int64_t first = n < rc.nslot ? n : rc.nslot;
+  if (warp == 0 && lane < kRingProducers)
+    for (int64_t k = lane; k < first; k += kRingProducers) issue(k);
+  // The coefficients are folded while the first rows are in flight.
+  for (int64_t i = threadIdx.x; i < nc; i += blockDim.x) {
+    const int64_t bb = i / C, c = i - bb * C;
+    float w[1] = {1.f}, bi[1] = {0.f}, sc[1] = {0.f}, sh[1] = {0.f};
+    if (p.w.ptr) load_chan<1>(p.w, 0, c, w);
+    if (p.b.ptr) load_chan<1>(p.b, 0, c, bi);
+    if (p.scale.ptr) load_chan<1>(p.scale, bb, c, sc);
+    if (p.shift.ptr) load_chan<1>(p.shift, bb, c, sh);
+    const float s1 = 1.f + sc[0];
+    coef[i] = w[0] * s1;
+    coef[nc + i] = bi[0] * s1 + sh[0];
+    if (p.g2.ptr) {
+      float g[1];
+      load_chan<1>(p.g2, bb, c, g);
+      coef[2 * nc + i] = g[0];
+    }
+  }
+  __syncthreads();
+  const int64_t nvec = C / VEC;
+  if (warp == 0) {
+    if (lane < kRingProducers) {
+      int64_t k = lane;
+      while (k < first) k += kRingProducers;
+      for (; k < n && !*abort_flag; k += kRingProducers) {
+        const int s = int(k % rc.nslot);
+        const uint32_t u = uint32_t(k / rc.nslot);  // >= 1: the slot's previous row is k - nslot
+        if (!ring_wait(&empty[s], (u - 1) & 1u, abort_flag, rc.wait_ns, false, &g_norm_status)) break;
+        issue(k);
+      }
+    }
+  } else {
+    for (int64_t k = warp - 1; k < n; k += NW) {
+      const int s = int(k % rc.nslot);
+      const uint32_t u = uint32_t(k / rc.nslot);
+      if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_norm_status)) break;
+      const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(s) * rc.row_bytes);
+      uint4 v[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t vi = lane + 32 * i;
+        v[i] = vi < nvec ? src[vi] : make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+      if (lane == 0) ring_arrive(&empty[s]);
+      float mean = 0.f, inv = 1.f;
+      if (p.norm == NORM_LAYER) {
+        // Shifted one-pass moments (shift = the row's first element), as in
+        // rownorm_kernel.
+        float2 a0[P];
+        unpack2(v[0], a0, T());
+        const float K = __shfl_sync(0xffffffffu, a0[0].x, 0);
+        const float2 nk = f2(-K);
+        float2 s1 = f2(0.f), s2 = f2(0.f);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          if (lane + 32 * i < nvec) {
+            float2 a[P];
+            unpack2(v[i], a, T());
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+              const float2 d = add2(a[q], nk);
+              s1 = add2(s1, d);
+              s2 = fma2(d, d, s2);
+            }
+          }
+        }
+        float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+          t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+        }
+        const float m1 = t1 / float(C);
+        mean = K + m1;
+        inv = 1.f / sqrtf(fmaxf(t2 / float(C) - m1 * m1, 0.f) + p.eps);
+      } else {
+        float2 acc = f2(0.f);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          float2 a[P];
+          unpack2(v[i], a, T());
+#pragma unroll
+          for (int q = 0; q < P; ++q) acc = fma2(a[q], a[q], acc);
+        }
+        float t = acc.x + acc.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        inv = 1.f / sqrtf(t / float(C) + p.eps);
+      }
+      const int64_t row = r0 + k;
+      const int64_t bb = p.nbatch > 1 ? row / p.rows_per_batch : 0;
+      T* yr = static_cast<T*>(p.y) + row_offset(p.ym, row);
+      const float2 nm = f2(-mean), inv2 = f2(inv);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t vi = lane + 32 * i;
+        if (vi >= nvec) continue;
+        const int64_t c0 = vi * VEC;
+        float2 a[P], o[P], fa[P], fb[P];
+        unpack2(v[i], a, T());
+#pragma unroll
+        for (int q = 0; q < P; ++q) o[q] = mul2(add2(a[q], nm), inv2);
+        const float* ca = coef + bb * C + c0;
+        const float* cb = ca + nc;
+        ld_pairs<P>(ca, fa);
+        ld_pairs<P>(cb, fb);
+#pragma unroll
+        for (int q = 0; q < P; ++q) o[q] = fma2(o[q], fa[q], fb[q]);
+        if (p.g2.ptr) {
+          ld_pairs<P>(cb + nc, fa);
+#pragma unroll
+          for (int q = 0; q < P; ++q) o[q] = mul2(fa[q], o[q]);
+        }
+        if (p.add_input) {
+#pragma unroll
+          for (int q = 0; q < P; ++q) o[q] = add2(o[q], a[q]);
+        }
+        st_act_raw(reinterpret_cast<uint4*>(yr + c0), pack2(o, T()));
+      }
+    }
+  }
+  __syncthreads();
+  // After an abort no copy into shared memory may still be in flight when the
+  // block exits: each producer lane waits (bounded) for the last row it
+  // issued into each of its slots.
+  if (*abort_flag && warp == 0 && lane < kRingProducers && last >= 0) {
+    for (int s = lane; s < rc.nslot; s += kRingProducers) {
+      if (last < s) continue;
+      const int64_t ks = last - ((last - s) % rc.nslot);  // newest row of slot s
+      ring_wait(&full[s], uint32_t(ks / rc.nslot) & 1u, abort_flag, rc.wait_ns, true, &g_norm_status);
+    }
+  }
+}
+
 // Resident blocks of one kernel instance on the whole device (one full wave).
 constexpr size_t kStageMax = 48 * 1024;  // shared-memory budget of the folded coefficients
 
@@ -481,6 +678,49 @@ static bool pick_geometry(int64_t nvec, bool scalar, int* G, int* NV) {
   *G = g;
   *NV = n;
   return n <= 8;
+}
+
+// Ring path selection (rowring_kernel): LN / RMS without a residual branch,
+// 16-byte vectors, rows of at most 8 KB, enough rows for every SM.
+constexpr int64_t kRingMinRows = 4096;
+
+template <typename T, int NV, int NW>
+static int launch_ring(const RowNormParams& p, const RingCfg& rc, size_t smem, cudaStream_t s) {
+  auto k = rowring_kernel<T, NV, NW>;
+  if (set_smem_limit(reinterpret_cast<const void*>(k), int(smem)) != cudaSuccess) return -1;
+  int64_t grid = (p.rows + NW - 1) / NW;
+  if (grid > sm_count()) grid = sm_count();
+  k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);
+  return 0;
+}
+
+// Returns 1 when the ring kernel was launched, 0 when the request is outside
+// its envelope, -1 on a CUDA error.
+template <typename T>
+static int try_ring(const RowNormParams& p, cudaStream_t s) {
+  const int es = int(sizeof(T));
+  const int vec = 16 / es;
+  const uint32_t row_bytes = uint32_t(p.C * es);
+  if (p.rows < kRingMinRows || row_bytes > 8192 || p.C % vec) return 0;
+  const int64_t nv = (p.C / vec + 31) / 32;
+  RingCfg rc{};
+  rc.row_bytes = row_bytes;
+  rc.coef_bytes = (size_t(p.nbatch) * size_t(p.C) * 4 * (p.g2.ptr ? 3 : 2) + 127) & ~size_t(127);
+  if (rc.coef_bytes > 64 * 1024) return 0;
+  const size_t bar_bytes = size_t(2) * kRingMaxSlots * 8 + 16;
+  int64_t ns = int64_t((kRingSmem - rc.coef_bytes - bar_bytes) / row_bytes);
+  if (ns > kRingMaxSlots) ns = kRingMaxSlots;
+  ns -= ns % kRingProducers;
+  if (ns < 2 * kRingProducers) return 0;
+  rc.nslot = int(ns);
+  rc.wait_ns = 2000000000ull;
+  const size_t smem = rc.coef_bytes + size_t(rc.nslot) * row_bytes + size_t(2) * rc.nslot * 8 + 16;
+  int rcode;
+  if (nv <= 2) rcode = launch_ring<T, 2, 24>(p, rc, smem, s);
+  else if (nv <= 4) rcode = launch_ring<T, 4, 24>(p, rc, smem, s);
+  else if (nv <= 8) rcode = launch_ring<T, 8, 24>(p, rc, smem, s);
+  else rcode = launch_ring<T, 16, 16>(p, rc, smem, s);
+  return rcode == 0 ? 1 : -1;
 }
 
 struct RowNormArgs {
@@ -574,10 +814,17 @@ static int run_rownorm(const RowNormArgs& a, cudaStream_t stream) {
     const size_t need = size_t(p.nbatch) * size_t(p.C) * sizeof(float) * (p.g2.ptr ? 3 : 2);
     if (need <= kStageMax) smem = need;
   }
-  L3D_DISPATCH_FLOAT(a.x->dtype, T, {
-    if (vec_ok) launch_rownorm<T, Vec16<T>::N>(p, G, NV, smem, stream);
-    else launch_rownorm<T, 1>(p, G, NV, smem, stream);
-  });
+  int ring = 0;
+  if (vec_ok && !a.h && !a.r_out && p.norm != NORM_NONE && smem) {
+    L3D_DISPATCH_FLOAT(a.x->dtype, T, { ring = try_ring<T>(p, stream); });
+    if (ring < 0) return fail(L3D_E_CUDA, "%s: cannot reserve the ring kernel's shared memory", op);
+  }
+  if (!ring) {
+    L3D_DISPATCH_FLOAT(a.x->dtype, T, {
+      if (vec_ok) launch_rownorm<T, Vec16<T>::N>(p, G, NV, smem, stream);
+      else launch_rownorm<T, 1>(p, G, NV, smem, stream);
+    });
+  }
   return check_launch(op);
 }
 
@@ -647,3 +894,14 @@ extern "C" int l3d_rms_norm_heads(const l3d_tensor* x, const l3d_tensor* weight,
   a.norm = NORM_RMS; a.op = "l3d_rms_norm_heads"; a.batch_dims = 0;
   return run_rownorm(a, reinterpret_cast<cudaStream_t>(stream));
 }
+
+namespace l3d {
+cudaError_t norm_status_read(int* status, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_norm_status, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_norm_status, &zero, sizeof(int));
+  }
+  return e;
+}
+}  // namespace l3d

@@ -20,6 +20,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "ring.cuh"
 
 namespace l3d {
 
@@ -405,6 +406,74 @@ __device__ __forceinline__ void unpack8(const Pack8<T>& r, float (&f)[8]) {
   }
 }
 
+// One 128-bit lane chunk of a head in the packed 16-bit path: four rotation
+// pairs (re_k, im_k) of `u`, worked on as (re, re) / (im, im) float pairs.
+// With `g` (gamma * sqrt(D) staged de-interleaved, this lane's 8 values) the
+// head is L2-normalised first: the sum of squares is reduced over the LPH
+// lanes of the head (all lanes of the warp call this together).  `valid`:
+// the lane holds a real chunk.  Returns the rotated chunk, rounded to T.
+template <typename T, int LPH>
+__device__ __forceinline__ uint4 rope3d_pk_chunk(const uint4& u, const float (&cs)[4],
+                                                 const float (&sn)[4], const float* g,
+                                                 bool valid) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float2 re2[2], im2[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      re2[q] = make_float2(__uint_as_float(w[2 * q] << 16), __uint_as_float(w[2 * q + 1] << 16));
+      im2[q] = make_float2(__uint_as_float(w[2 * q] & 0xffff0000u),
+                           __uint_as_float(w[2 * q + 1] & 0xffff0000u));
+    } else {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * q]));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * q + 1]));
+      re2[q] = make_float2(a.x, c.x);
+      im2[q] = make_float2(a.y, c.y);
+    }
+  }
+  if (g) {
+    float2 acc = mul2(re2[0], re2[0]);
+    acc = fma2(im2[0], im2[0], acc);
+    acc = fma2(re2[1], re2[1], acc);
+    acc = fma2(im2[1], im2[1], acc);
+    float ss = acc.x + acc.y;
+#pragma unroll
+    for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    // 1 / clamp(||x||, 1e-12, 1e30) = rsqrt(clamp(||x||^2, 1e-24, 1e60)).
+    const float2 rn = f2(rsqrtf(fminf(fmaxf(ss, 1e-24f), 1e30f * 1e30f)));
+    if (valid) {
+      const float4* gp = reinterpret_cast<const float4*>(g);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float4 gq = gp[q];
+        re2[q] = mul2(re2[q], mul2(make_float2(gq.x, gq.y), rn));
+        im2[q] = mul2(im2[q], mul2(make_float2(gq.z, gq.w), rn));
+      }
+    }
+  }
+  // (re, im) -> (re c - im s, re s + im c).
+  uint32_t ow[4];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const float2 c2 = make_float2(cs[2 * q], cs[2 * q + 1]);
+    const float2 s2 = make_float2(sn[2 * q], sn[2 * q + 1]);
+    const float2 ore = fma2(re2[q], c2, mul2(im2[q], make_float2(-s2.x, -s2.y)));
+    const float2 oim = fma2(re2[q], s2, mul2(im2[q], c2));
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(ore.x, oim.x);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(ore.y, oim.y);
+      ow[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
+      ow[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
+    } else {
+      __half2 h0 = __floats2half2_rn(ore.x, oim.x);
+      __half2 h1 = __floats2half2_rn(ore.y, oim.y);
+      ow[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
+      ow[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
+    }
+  }
+  return make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
 // EPL elements per lane (8: 16-byte path; 2: one pair per lane), LPH lanes per
 // head row (D / EPL rounded up to a power of two).  gamma * sqrt(D) is staged
 // once per block in shared memory (dynamic, H * D floats) when present.
@@ -501,65 +570,12 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope3d_kernel(con
         const int h = hb + it * HPI + hg;
         const bool valid = h < p.H && lane_on;
         if constexpr (PK) {
-          // Pairs k = 0..3 of the lane (word k = (re_k, im_k)) as
-          // re2[q] = (re_2q, re_2q+1) and im2[q] = (im_2q, im_2q+1).
-          const uint32_t w[4] = {pk[it].u[0].x, pk[it].u[0].y, pk[it].u[0].z, pk[it].u[0].w};
-          float2 re2[2], im2[2];
+          float c4[4], s4[4];
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-              re2[q] = make_float2(__uint_as_float(w[2 * q] << 16), __uint_as_float(w[2 * q + 1] << 16));
-              im2[q] = make_float2(__uint_as_float(w[2 * q] & 0xffff0000u),
-                                   __uint_as_float(w[2 * q + 1] & 0xffff0000u));
-            } else {
-              const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * q]));
-              const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * q + 1]));
-              re2[q] = make_float2(a.x, c.x);
-              im2[q] = make_float2(a.y, c.y);
-            }
-          }
-          if (p.gamma) {
-            float2 acc = mul2(re2[0], re2[0]);
-            acc = fma2(im2[0], im2[0], acc);
-            acc = fma2(re2[1], re2[1], acc);
-            acc = fma2(im2[1], im2[1], acc);
-            float ss = acc.x + acc.y;
-#pragma unroll
-            for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            // 1 / clamp(||x||, 1e-12, 1e30) = rsqrt(clamp(||x||^2, 1e-24, 1e60)).
-            const float2 rn = f2(rsqrtf(fminf(fmaxf(ss, 1e-24f), 1e30f * 1e30f)));
-            if (valid) {
-              const float4* g = reinterpret_cast<const float4*>(gsm + h * p.D + m * EPL);
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                const float4 gq = g[q];
-                re2[q] = mul2(re2[q], mul2(make_float2(gq.x, gq.y), rn));
-                im2[q] = mul2(im2[q], mul2(make_float2(gq.z, gq.w), rn));
-              }
-            }
-          }
-          // (re, im) -> (re c - im s, re s + im c).
-          uint32_t ow[4];
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const float2 c2 = make_float2(cs[2 * q], cs[2 * q + 1]);
-            const float2 s2 = make_float2(sn[2 * q], sn[2 * q + 1]);
-            const float2 ore = fma2(re2[q], c2, mul2(im2[q], make_float2(-s2.x, -s2.y)));
-            const float2 oim = fma2(re2[q], s2, mul2(im2[q], c2));
-            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-              __nv_bfloat162 h0 = __floats2bfloat162_rn(ore.x, oim.x);
-              __nv_bfloat162 h1 = __floats2bfloat162_rn(ore.y, oim.y);
-              ow[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
-              ow[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
-            } else {
-              __half2 h0 = __floats2half2_rn(ore.x, oim.x);
-              __half2 h1 = __floats2half2_rn(ore.y, oim.y);
-              ow[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
-              ow[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
-            }
-          }
-          if (valid)
-            st_act_raw(reinterpret_cast<uint4*>(yt + int64_t(h) * p.ysh), make_uint4(ow[0], ow[1], ow[2], ow[3]));
+          for (int k = 0; k < 4; ++k) { c4[k] = cs[k]; s4[k] = sn[k]; }
+          const uint4 o = rope3d_pk_chunk<T, LPH>(pk[it].u[0], c4, s4,
+                                                  p.gamma ? gsm + h * p.D + m * EPL : nullptr, valid);
+          if (valid) st_act_raw(reinterpret_cast<uint4*>(yt + int64_t(h) * p.ysh), o);
           continue;
         }
         float v[EPL];
@@ -603,6 +619,200 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope3d_kernel(con
       }
     }
   }
+}
+
+// ----------------------------------------------------------- ring variant
+// 16-bit activations with D = 128 and the heads of a token contiguous (a row
+// of H * 128 elements, e.g. the bench's [T, C] rows or a [B, L, H, D] q/k):
+// one CTA per SM streams its block of tokens through a ring of shared-memory
+// slots filled by bulk copies (one per token row, eight producer lanes),
+// consumer warps take every NW-th token, copy its row into registers,
+// release the slot and apply the same per-chunk arithmetic as rope3d_kernel
+// (rope3d_pk_chunk), so the two give identical bits.  Bounded waits; on expiry
+// status 5 goes to g_rope_status and the block drains its copies.
+__device__ int g_rope_status;
+constexpr int kRopeRingProducers = 8;
+constexpr int kRopeRingMaxSlots = 96;
+constexpr size_t kRopeRingSmem = 200 * 1024;
+constexpr int64_t kRopeRingMinRows = 4096;
+
+struct RopeRingCfg {
+  int nslot;            // multiple of kRopeRingProducers
+  uint32_t row_bytes;   // H * D * 2
+  size_t g_bytes;       // staged gamma, 128-aligned
+  uint64_t wait_ns;
+};
+
+template <typename T, int NV, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 1)
+    rope3d_ring_kernel(const Rope3dParams p, const RopeRingCfg rc) {
+  constexpr int LPH = 16, EPL = 8, NP = 4;
+  extern __shared__ __align__(128) unsigned char rsm[];
+  float* gsm = reinterpret_cast<float*>(rsm);  // [H, D] gamma * sqrt(D), de-interleaved
+  unsigned char* slots = rsm + rc.g_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + size_t(rc.nslot) * rc.row_bytes);
+  uint64_t* empty = full + rc.nslot;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + rc.nslot);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = lane % LPH, hg = lane / LPH;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < rc.nslot; ++s) {
+      ring_bar_init(&full[s], 1);
+      ring_bar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    ring_init_fence();
+  }
+  __syncthreads();
+  const int64_t tokens = p.B * p.L;
+  const int64_t per = (tokens + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = int64_t(blockIdx.x) * per;
+  const int64_t n = r0 < tokens ? (tokens - r0 < per ? tokens - r0 : per) : 0;
+  int64_t last = -1;
+  auto issue = [&](int64_t k) {
+    const int s = int(k % rc.nslot);
+    const int64_t tok = r0 + k, b = tok / p.L, l = tok - b * p.L;
+    ring_load(slots + size_t(s) * rc.row_bytes,
+              static_cast<const T*>(p.x) + p.xbase + b * p.xsb + l * p.xsl, rc.row_bytes, &full[s]);
+    last = k;
+  };
+  const int64_t first = n < rc.nslot ? n : rc.nslot;
+  if (warp == 0 && lane < kRopeRingProducers)
+    for (int64_t k = lane; k < first; k += kRopeRingProducers) issue(k);
+  if (p.gamma) {
+    for (int i = threadIdx.x; i < p.H * p.D; i += blockDim.x) {
+      const int h = i / p.D, d = i - h * p.D;
+      gsm[h * p.D + (d & ~3) + ((d & 1) << 1) + ((d >> 1) & 1)] = p.gamma[int64_t(h) * p.gsh + d] * p.scale;
+    }
+  }
+  __syncthreads();
+  const int half = p.D / 2;
+  if (warp == 0) {
+    if (lane < kRopeRingProducers) {
+      int64_t k = lane;
+      while (k < first) k += kRopeRingProducers;
+      for (; k < n && !*abort_flag; k += kRopeRingProducers) {
+        const int s = int(k % rc.nslot);
+        const uint32_t u = uint32_t(k / rc.nslot);
+        if (!ring_wait(&empty[s], (u - 1) & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
+        issue(k);
+      }
+    }
+  } else {
+    float fr[NP];
+    int axis[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+      const int pr = m * NP + k;
+      const int a = p.freq_dim > 0 ? pr / p.freq_dim : 3;
+      axis[k] = (p.coords && pr < half && a < 3) ? a : -1;
+      fr[k] = axis[k] >= 0 ? inv_freq_f32(p.theta, float(pr - a * p.freq_dim), float(p.freq_dim))
+                           : 0.f;
+    }
+    const int64_t nvec = int64_t(p.H) * (p.D / EPL);
+    for (int64_t k = warp - 1; k < n; k += NW) {
+      const int s = int(k % rc.nslot);
+      const uint32_t u = uint32_t(k / rc.nslot);
+      if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
+      const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(s) * rc.row_bytes);
+      uint4 v[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t vi = lane + 32 * i;
+        v[i] = vi < nvec ? src[vi] : make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+      if (lane == 0) ring_arrive(&empty[s]);
+      const int64_t tok = r0 + k, b = tok / p.L, l = tok - b * p.L;
+      float cs[NP], sn[NP];
+      if (p.use_table) {
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+          const int pr = m * NP + q;
+          cs[q] = pr < half ? __ldg(p.cost + p.tcbase + l * p.tcsl + pr) : 1.f;
+          sn[q] = pr < half ? __ldg(p.sint + p.tsbase + l * p.tssl + pr) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+          if (axis[q] >= 0) {
+            const float cv = load_index_f(p.coords, p.coord_dtype, p.cbase + l * p.csl + axis[q] * p.csa);
+            sincos_t<T>(__fmul_rn(cv, fr[q]), &sn[q], &cs[q]);
+          } else {
+            cs[q] = 1.f;
+            sn[q] = 0.f;
+          }
+        }
+      }
+      T* yt = static_cast<T*>(p.y) + p.ybase + b * p.ysb + l * p.ysl + m * EPL;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (2 * i >= p.H) break;  // warp-uniform
+        const int h = 2 * i + hg;
+        const bool valid = h < p.H;
+        const uint4 o = rope3d_pk_chunk<T, LPH>(v[i], cs, sn,
+                                                p.gamma ? gsm + h * p.D + m * EPL : nullptr, valid);
+        if (valid) st_act_raw(reinterpret_cast<uint4*>(yt + int64_t(h) * p.D), o);
+      }
+    }
+  }
+  __syncthreads();
+  if (*abort_flag && warp == 0 && lane < kRopeRingProducers && last >= 0) {
+    for (int s = lane; s < rc.nslot; s += kRopeRingProducers) {
+      if (last < s) continue;
+      const int64_t ks = last - ((last - s) % rc.nslot);
+      ring_wait(&full[s], uint32_t(ks / rc.nslot) & 1u, abort_flag, rc.wait_ns, true, &g_rope_status);
+    }
+  }
+}
+
+template <typename T, int NV, int NW>
+static int launch_rope3d_ring(const Rope3dParams& p, const RopeRingCfg& rc, size_t smem,
+                              cudaStream_t s) {
+  auto k = rope3d_ring_kernel<T, NV, NW>;
+  if (set_smem_limit(reinterpret_cast<const void*>(k), int(smem)) != cudaSuccess) return -1;
+  int64_t grid = (p.B * p.L + NW - 1) / NW;
+  if (grid > sm_count()) grid = sm_count();
+  k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);
+  return 0;
+}
+
+// 1: launched; 0: outside the ring kernel's envelope; -1: CUDA error.
+template <typename T>
+static int try_rope3d_ring(const Rope3dParams& p, cudaStream_t s) {
+  if constexpr (sizeof(T) != 2) {
+    return 0;
+  } else {
+    if (p.D != 128 || p.xsh != p.D || p.ysh != p.D || p.B * p.L < kRopeRingMinRows) return 0;
+    const uint32_t row_bytes = uint32_t(p.H) * 128u * 2u;
+    if (p.H < 1 || row_bytes > 8192) return 0;
+    RopeRingCfg rc{};
+    rc.row_bytes = row_bytes;
+    rc.g_bytes = p.gamma ? ((size_t(p.H) * 128 * 4 + 127) & ~size_t(127)) : 0;
+    const size_t bar_bytes = size_t(2) * kRopeRingMaxSlots * 8 + 16;
+    int64_t ns = int64_t((kRopeRingSmem - rc.g_bytes - bar_bytes) / row_bytes);
+    if (ns > kRopeRingMaxSlots) ns = kRopeRingMaxSlots;
+    ns -= ns % kRopeRingProducers;
+    if (ns < 2 * kRopeRingProducers) return 0;
+    rc.nslot = int(ns);
+    rc.wait_ns = 2000000000ull;
+    const size_t smem = rc.g_bytes + size_t(rc.nslot) * row_bytes + size_t(2) * rc.nslot * 8 + 16;
+    const int nv = (p.H + 1) / 2;
+    int r;
+    if (nv <= 4) r = launch_rope3d_ring<T, 4, 24>(p, rc, smem, s);
+    else if (nv <= 8) r = launch_rope3d_ring<T, 8, 24>(p, rc, smem, s);
+    else r = launch_rope3d_ring<T, 16, 16>(p, rc, smem, s);
+    return r == 0 ? 1 : -1;
+  }
+}
+
+cudaError_t rope_status_read(int* status, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_rope_status, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_rope_status, &zero, sizeof(int));
+  }
+  return e;
 }
 
 __global__ void rope3d_tables_kernel(int64_t L, const void* coords, int cdt, int64_t cbase,
@@ -878,7 +1088,13 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
   const size_t smem = p.gamma ? size_t(p.H) * size_t(p.D) * sizeof(float) : 0;
   if (smem > 48 * 1024) return fail(L3D_E_UNSUPPORTED, "%s: gamma [H, D] above 12288 values", op);
   const int blocks = launch_grid_warps(p.B * p.L);
+  int ring = 0;
   if (fast) {
+    L3D_DISPATCH_FLOAT(x->dtype, T, { ring = try_rope3d_ring<T>(p, stream); });
+    if (ring < 0) return fail(L3D_E_CUDA, "%s: cannot reserve the ring kernel's shared memory", op);
+  }
+  if (ring) {
+  } else if (fast) {
     const int lph = p.D / 8 <= 4 ? 4 : p.D / 8 <= 8 ? 8 : p.D / 8 <= 16 ? 16 : 32;
     L3D_DISPATCH_FLOAT(x->dtype, T, {
       switch (lph) {

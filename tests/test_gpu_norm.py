@@ -125,3 +125,36 @@ def test_empty_rows_are_noops(ops, dev):
 
     x = torch.empty((0, 64), device=dev)
     assert ops.layer_norm(x).shape == (0, 64)
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("C,affine", [(2048, False), (1536, True), (64, True), (4096, False)])
+def test_layer_norm_ring_path_rows(ops, orc, dev, dt, C, affine):
+    """Inputs of at least 4096 rows take the shared-memory ring kernel (bulk
+    copies of whole rows); rows of up to 8 KB, with and without affine
+    vectors, modulation and gate, and the kernels' status word stays 0."""
+    import ctypes
+
+    if C * {"f32": 4, "bf16": 2, "f16": 2}[dt] > 8192:
+        C = 2048
+    r = rng(7)
+    T = 5000
+    x, xv = to_dev(r.standard_normal((T, C)), dt, dev)
+    w = b = wv = bv = None
+    if affine:
+        w, wv = to_dev(1 + 0.02 * r.standard_normal(C), dt, dev)
+        b, bv = to_dev(0.02 * r.standard_normal(C), dt, dev)
+    y = ops.layer_norm(x, w, b, eps=1e-6)
+    assert_close(y.float().cpu().numpy(), orc.layer_norm(xv, wv, bv, 1e-6), dt, "ring LN")
+    g, gv = to_dev(0.1 * r.standard_normal(C), dt, dev)
+    sh, shv = to_dev(0.1 * r.standard_normal(C), dt, dev)
+    y2 = ops.layer_norm_modulate(x, sh, None, gate=g, add_input=True, eps=1e-6)
+    ref2 = orc.layer_norm_modulate(xv.reshape(1, T, C), shift=shv, gate=gv, add_input=True,
+                                   eps=1e-6).reshape(T, C)
+    assert_close(y2.float().cpu().numpy(), ref2, dt, "ring LN+modulate+gate")
+    import torch
+
+    torch.cuda.synchronize()
+    st = ctypes.c_int(-1)
+    assert ops._lib.lib().l3d_kernel_status(ctypes.byref(st), 1) == 0
+    assert st.value == 0

@@ -24,6 +24,14 @@
 
 namespace l3d {
 
+// Ring kernels (rope2d_ring_kernel, rope3d_ring_kernel): the per-device
+// status word of their bounded waits and their shared-memory geometry.
+__device__ int g_rope_status;
+constexpr int kRopeRingProducers = 8;
+constexpr int kRopeRingMaxSlots = 96;
+constexpr size_t kRopeRingSmem = 200 * 1024;
+constexpr int64_t kRopeRingMinRows = 4096;
+
 // --------------------------------------------------------------------- helpers
 __device__ __forceinline__ float inv_freq_f32(float theta, float num, float den) {
   const float e = __fdiv_rn(num, den);
@@ -191,6 +199,54 @@ __device__ __forceinline__ void store4x2(T* p, const float2 (&v)[2]) {
   }
 }
 
+// One lane's two quarter-chunks of a head (A = 4 elements at 32h + 4k, B =
+// A + 16, packed) through the per-head LayerNorm (the head's 8 lanes reduce
+// together, xor shuffles 1, 2, 4: mean, then the centred sum of squares) and
+// the rotation with the folded coefficients `k`.  All lanes of the warp call
+// it together.
+template <typename T>
+__device__ __forceinline__ void rope2d_chunks(const typename Raw4<T>::type& ra,
+                                              const typename Raw4<T>::type& rb,
+                                              const Rope2dCoef& k, int do_norm, float eps,
+                                              float2 (&oa)[2], float2 (&ob)[2]) {
+  float2 a[2], bv[2];
+  unpack4x2<T>(ra, a);
+  unpack4x2<T>(rb, bv);
+  if (do_norm) {
+    const float2 s2 = __fadd2_rn(__fadd2_rn(a[0], a[1]), __fadd2_rn(bv[0], bv[1]));
+    float sum = s2.x + s2.y;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    const float2 nm = f2(-sum * (1.0f / 64.0f));
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      a[pr] = __fadd2_rn(a[pr], nm);
+      bv[pr] = __fadd2_rn(bv[pr], nm);
+    }
+    float2 q2 = __fmul2_rn(a[0], a[0]);
+    q2 = __ffma2_rn(a[1], a[1], q2);
+    q2 = __ffma2_rn(bv[0], bv[0], q2);
+    q2 = __ffma2_rn(bv[1], bv[1], q2);
+    float ss = q2.x + q2.y;
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    const float var = ss * (1.0f / 64.0f) + eps;
+    const float2 inv = f2(sizeof(T) == 2 ? rsqrtf(var) : 1.f / sqrtf(var));
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      a[pr] = __fmul2_rn(a[pr], inv);
+      bv[pr] = __fmul2_rn(bv[pr], inv);
+    }
+  }
+#pragma unroll
+  for (int pr = 0; pr < 2; ++pr) {
+    oa[pr] = __ffma2_rn(a[pr], k.k1a[pr], __ffma2_rn(bv[pr], k.k2a[pr], k.k0a[pr]));
+    ob[pr] = __ffma2_rn(bv[pr], k.k1b[pr], __ffma2_rn(a[pr], k.k2b[pr], k.k0b[pr]));
+  }
+}
+
 // One warp per token; 8 lanes per 64-wide head row, 4 heads per iteration.
 // Lane j (0..7) of a head owns the two quarter-chunks that rotate into each
 // other: elements A = 32h + 4k + t and B = A + 16 (h = j / 4, k = j % 4,
@@ -285,43 +341,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope2d_kernel(con
         for (int it = 0; it < MAXIT; ++it) {
           if (hb + it * 4 >= p.H) break;  // warp-uniform
           const int h = hb + it * 4 + hg;
-          float2 a[2], bv[2];
-          unpack4x2<T>(ra[it], a);
-          unpack4x2<T>(rb[it], bv);
-          if (p.do_norm) {
-            const float2 s2 = __fadd2_rn(__fadd2_rn(a[0], a[1]), __fadd2_rn(bv[0], bv[1]));
-            float sum = s2.x + s2.y;
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-            const float2 nm = f2(-sum * (1.0f / 64.0f));
-#pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-              a[pr] = __fadd2_rn(a[pr], nm);
-              bv[pr] = __fadd2_rn(bv[pr], nm);
-            }
-            float2 q2 = __fmul2_rn(a[0], a[0]);
-            q2 = __ffma2_rn(a[1], a[1], q2);
-            q2 = __ffma2_rn(bv[0], bv[0], q2);
-            q2 = __ffma2_rn(bv[1], bv[1], q2);
-            float ss = q2.x + q2.y;
-            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-            ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-            const float var = ss * (1.0f / 64.0f) + p.eps;
-            const float2 inv = f2(sizeof(T) == 2 ? rsqrtf(var) : 1.f / sqrtf(var));
-#pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-              a[pr] = __fmul2_rn(a[pr], inv);
-              bv[pr] = __fmul2_rn(bv[pr], inv);
-            }
-          }
           float2 oa[2], ob[2];
-#pragma unroll
-          for (int pr = 0; pr < 2; ++pr) {
-            oa[pr] = __ffma2_rn(a[pr], k.k1a[pr], __ffma2_rn(bv[pr], k.k2a[pr], k.k0a[pr]));
-            ob[pr] = __ffma2_rn(bv[pr], k.k1b[pr], __ffma2_rn(a[pr], k.k2b[pr], k.k0b[pr]));
-          }
+          rope2d_chunks<T>(ra[it], rb[it], k, p.do_norm, p.eps, oa, ob);
           if (h < p.H) {
             T* dst = dst0 + int64_t(h) * ov.sh;
             store4x2<T>(dst, oa);
@@ -331,6 +352,212 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope2d_kernel(con
       }
     }
   }
+}
+
+// ----------------------------------------------------------- ring variant
+// q (and k) with a token's heads contiguous (head stride 64, e.g. views of a
+// [B, N, 3, H, 64] projection or of [T, C] rows) and at least 4096 tokens:
+// one CTA per SM streams its block of tokens through shared-memory slots
+// (one bulk copy per tensor row, eight producer lanes); each consumer warp
+// copies its token's chunks (the rope2d_kernel lane layout) into registers,
+// releases the slot and applies rope2d_chunks (identical bits).  Bounded
+// waits; on expiry status 5 goes to g_rope_status and the block drains its
+// copies.
+struct Rope2dRingCfg {
+  int nslot;            // multiple of kRopeRingProducers
+  uint32_t row_bytes;   // H * 64 * element size (one tensor)
+  uint32_t slot_bytes;  // ntensor * row_bytes
+  uint64_t wait_ns;
+};
+
+template <typename T, int NIT, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 1)
+    rope2d_ring_kernel(const Rope2dParams p, const Rope2dRingCfg rc) {
+  extern __shared__ __align__(128) unsigned char rsm2[];
+  __shared__ __align__(16) float aff[2][2][64];
+  unsigned char* slots = rsm2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + size_t(rc.nslot) * rc.slot_bytes);
+  uint64_t* empty = full + rc.nslot;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + rc.nslot);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = lane & 7, hg = lane >> 3;
+  const int ea = 32 * (j >> 2) + 4 * (j & 3);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < rc.nslot; ++s) {
+      ring_bar_init(&full[s], 1);
+      ring_bar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    ring_init_fence();
+  }
+  __syncthreads();
+  const int64_t tokens = p.B * p.N;
+  const int64_t per = (tokens + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = int64_t(blockIdx.x) * per;
+  const int64_t n = r0 < tokens ? (tokens - r0 < per ? tokens - r0 : per) : 0;
+  int64_t last = -1;
+  auto issue = [&](int64_t k) {
+    const int s = int(k % rc.nslot);
+    const int64_t tok = r0 + k, b = tok / p.N, nn = tok - b * p.N;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     smem_addr(&full[s])),
+                 "r"(rc.slot_bytes)
+                 : "memory");
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t >= p.ntensor) break;
+      const HeadView& iv = p.in[t];
+      const T* src = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + nn * iv.sn;
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+              "r"(smem_addr(slots + size_t(s) * rc.slot_bytes + size_t(t) * rc.row_bytes)),
+          "l"(src), "r"(rc.row_bytes), "r"(smem_addr(&full[s]))
+          : "memory");
+    }
+    last = k;
+  };
+  const int64_t first = n < rc.nslot ? n : rc.nslot;
+  if (warp == 0 && lane < kRopeRingProducers)
+    for (int64_t k = lane; k < first; k += kRopeRingProducers) issue(k);
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    const int t = i >> 7, wb = (i >> 6) & 1, e = i & 63;
+    float v = wb ? 0.f : 1.f;
+    if (t < p.ntensor && p.do_norm) {
+      const ChanVec& cv = wb ? p.b[t] : p.w[t];
+      if (cv.ptr) {
+        float one[1];
+        load_chan<1>(cv, 0, e, one);
+        v = one[0];
+      }
+    }
+    aff[t][wb][e] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane < kRopeRingProducers) {
+      int64_t k = lane;
+      while (k < first) k += kRopeRingProducers;
+      for (; k < n && !*abort_flag; k += kRopeRingProducers) {
+        const int s = int(k % rc.nslot);
+        const uint32_t u = uint32_t(k / rc.nslot);
+        if (!ring_wait(&empty[s], (u - 1) & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
+        issue(k);
+      }
+    }
+  } else {
+    const float invf = inv_freq_f32(p.theta, float(2 * (lane & 15)), 32.0f);
+    using R = typename Raw4<T>::type;
+    for (int64_t k = warp - 1; k < n; k += NW) {
+      const int s = int(k % rc.nslot);
+      const uint32_t u = uint32_t(k / rc.nslot);
+      if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
+      R ra[2][NIT], rb[2][NIT];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const T* row = reinterpret_cast<const T*>(slots + size_t(s) * rc.slot_bytes +
+                                                  size_t(t) * rc.row_bytes);
+#pragma unroll
+        for (int it = 0; it < NIT; ++it) {
+          const int h = 4 * it + hg;
+          if (t < p.ntensor && h < p.H) {
+            ra[t][it] = *reinterpret_cast<const R*>(row + h * 64 + ea);
+            rb[t][it] = *reinterpret_cast<const R*>(row + h * 64 + ea + 16);
+          } else {
+            ra[t][it] = rb[t][it] = R{};
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) ring_arrive(&empty[s]);
+      const int64_t tok = r0 + k, b = tok / p.N, nn = tok - b * p.N;
+      float c[4], sn[4];
+      if (p.use_table) {
+        const float* cp = p.cosp + p.cbase + b * p.csb + nn * p.csn + ea;
+        const float* sp = p.sinp + p.sbase + b * p.ssb + nn * p.ssn + ea;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { c[i] = __ldg(cp + i); sn[i] = -__ldg(sp + i); }
+      } else {
+        const float pos = load_index_f(p.pos, p.pos_dtype,
+                                       p.pbase + b * p.psb + nn * p.psn + (lane >> 4) * p.psc);
+        float sv, cv;
+        sincos_t<T>(__fmul_rn(pos, invf), &sv, &cv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          c[i] = __shfl_sync(0xffffffffu, cv, 4 * j + i);
+          sn[i] = __shfl_sync(0xffffffffu, sv, 4 * j + i);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t >= p.ntensor) break;
+        const HeadView& ov = p.out[t];
+        T* dst0 = static_cast<T*>(ov.data) + ov.base + b * ov.sb + nn * ov.sn + ea;
+        Rope2dCoef kc;
+        rope2d_coef(aff[t], ea, c, sn, kc);
+#pragma unroll
+        for (int it = 0; it < NIT; ++it) {
+          if (4 * it >= p.H) break;  // warp-uniform
+          const int h = 4 * it + hg;
+          float2 oa[2], ob[2];
+          rope2d_chunks<T>(ra[t][it], rb[t][it], kc, p.do_norm, p.eps, oa, ob);
+          if (h < p.H) {
+            T* dst = dst0 + int64_t(h) * ov.sh;
+            store4x2<T>(dst, oa);
+            store4x2<T>(dst + 16, ob);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (*abort_flag && warp == 0 && lane < kRopeRingProducers && last >= 0) {
+    for (int s = lane; s < rc.nslot; s += kRopeRingProducers) {
+      if (last < s) continue;
+      const int64_t ks = last - ((last - s) % rc.nslot);
+      ring_wait(&full[s], uint32_t(ks / rc.nslot) & 1u, abort_flag, rc.wait_ns, true, &g_rope_status);
+    }
+  }
+}
+
+template <typename T, int NIT, int NW>
+static int launch_rope2d_ring(const Rope2dParams& p, const Rope2dRingCfg& rc, size_t smem,
+                              cudaStream_t s) {
+  auto k = rope2d_ring_kernel<T, NIT, NW>;
+  if (set_smem_limit(reinterpret_cast<const void*>(k), int(smem)) != cudaSuccess) return -1;
+  int64_t grid = (p.B * p.N + NW - 1) / NW;
+  if (grid > sm_count()) grid = sm_count();
+  k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);
+  return 0;
+}
+
+// 1: launched; 0: outside the ring kernel's envelope; -1: CUDA error.
+template <typename T>
+static int try_rope2d_ring(const Rope2dParams& p, cudaStream_t s) {
+  if (p.B * p.N < kRopeRingMinRows || p.H > 32) return 0;
+  for (int t = 0; t < p.ntensor; ++t)
+    if (p.H > 1 && p.in[t].sh != 64) return 0;
+  const uint32_t row_bytes = uint32_t(p.H) * 64u * uint32_t(sizeof(T));
+  Rope2dRingCfg rc{};
+  rc.row_bytes = row_bytes;
+  rc.slot_bytes = row_bytes * uint32_t(p.ntensor);
+  if (rc.slot_bytes > 8192) return 0;
+  const size_t bar_bytes = size_t(2) * kRopeRingMaxSlots * 8 + 16;
+  int64_t ns = int64_t((kRopeRingSmem - bar_bytes) / rc.slot_bytes);
+  if (ns > kRopeRingMaxSlots) ns = kRopeRingMaxSlots;
+  ns -= ns % kRopeRingProducers;
+  if (ns < 2 * kRopeRingProducers) return 0;
+  rc.nslot = int(ns);
+  rc.wait_ns = 2000000000ull;
+  const size_t smem = size_t(rc.nslot) * rc.slot_bytes + size_t(2) * rc.nslot * 8 + 16;
+  int r;
+  if constexpr (sizeof(T) == 4) {
+    if (p.H <= 16) r = launch_rope2d_ring<T, 4, 12>(p, rc, smem, s);
+    else r = launch_rope2d_ring<T, 8, 8>(p, rc, smem, s);
+  } else {
+    if (p.H <= 16) r = launch_rope2d_ring<T, 4, 16>(p, rc, smem, s);
+    else r = launch_rope2d_ring<T, 8, 12>(p, rc, smem, s);
+  }
+  return r == 0 ? 1 : -1;
 }
 
 __global__ void rope2d_tables_kernel(int64_t B, int64_t N, const void* pos, int pos_dtype,
@@ -630,11 +857,6 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope3d_kernel(con
 // release the slot and apply the same per-chunk arithmetic as rope3d_kernel
 // (rope3d_pk_chunk), so the two give identical bits.  Bounded waits; on expiry
 // status 5 goes to g_rope_status and the block drains its copies.
-__device__ int g_rope_status;
-constexpr int kRopeRingProducers = 8;
-constexpr int kRopeRingMaxSlots = 96;
-constexpr size_t kRopeRingSmem = 200 * 1024;
-constexpr int64_t kRopeRingMinRows = 4096;
 
 struct RopeRingCfg {
   int nslot;            // multiple of kRopeRingProducers
@@ -948,8 +1170,13 @@ static int run_rope2d(const l3d_tensor* const* xs, const l3d_tensor* const* ws,
     p.cosp = static_cast<const float*>(cosf_t->data);
     p.sinp = static_cast<const float*>(sinf_t->data);
   }
-  const int blocks = launch_grid_warps(p.B * p.N);
-  L3D_DISPATCH_FLOAT(dt, T, { rope2d_kernel<T><<<blocks, 256, 0, stream>>>(p); });
+  int ring = 0;
+  L3D_DISPATCH_FLOAT(dt, T, { ring = try_rope2d_ring<T>(p, stream); });
+  if (ring < 0) return fail(L3D_E_CUDA, "%s: cannot reserve the ring kernel's shared memory", op);
+  if (!ring) {
+    const int blocks = launch_grid_warps(p.B * p.N);
+    L3D_DISPATCH_FLOAT(dt, T, { rope2d_kernel<T><<<blocks, 256, 0, stream>>>(p); });
+  }
   return check_launch(op);
 }
 

@@ -687,7 +687,8 @@ constexpr int64_t kRingMinRows = 4096;
 template <typename T, int NV, int NW>
 static int launch_ring(const RowNormParams& p, const RingCfg& rc, size_t smem, cudaStream_t s) {
   auto k = rowring_kernel<T, NV, NW>;
-  if (set_smem_limit(reinterpret_cast<const void*>(k), int(smem)) != cudaSuccess) return -1;
+  // The limit is set once per device to the most any launch of it uses.
+  if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRingSmem)) != cudaSuccess) return -1;
   int64_t grid = (p.rows + NW - 1) / NW;
   if (grid > sm_count()) grid = sm_count();
   k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);

@@ -523,7 +523,8 @@ template <typename T, int NIT, int NW>
 static int launch_rope2d_ring(const Rope2dParams& p, const Rope2dRingCfg& rc, size_t smem,
                               cudaStream_t s) {
   auto k = rope2d_ring_kernel<T, NIT, NW>;
-  if (set_smem_limit(reinterpret_cast<const void*>(k), int(smem)) != cudaSuccess) return -1;
+  // The limit is set once per device to the most any launch of it uses.
+  if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRopeRingSmem)) != cudaSuccess) return -1;
   int64_t grid = (p.B * p.N + NW - 1) / NW;
   if (grid > sm_count()) grid = sm_count();
   k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);
@@ -992,7 +993,8 @@ template <typename T, int NV, int NW>
 static int launch_rope3d_ring(const Rope3dParams& p, const RopeRingCfg& rc, size_t smem,
                               cudaStream_t s) {
   auto k = rope3d_ring_kernel<T, NV, NW>;
-  if (set_smem_limit(reinterpret_cast<const void*>(k), int(smem)) != cudaSuccess) return -1;
+  // The limit is set once per device to the most any launch of it uses.
+  if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRopeRingSmem)) != cudaSuccess) return -1;
   int64_t grid = (p.B * p.L + NW - 1) / NW;
   if (grid > sm_count()) grid = sm_count();
   k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);

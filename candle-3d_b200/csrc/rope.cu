@@ -447,7 +447,16 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
   } else {
     const float invf = inv_freq_f32(p.theta, float(2 * (lane & 15)), 32.0f);
     using R = typename Raw4<T>::type;
+    // This lane's position of the warp's next token, loaded one token ahead.
+    auto load_pos = [&](int64_t kk) {
+      if (p.use_table || kk >= n) return 0.f;
+      const int64_t tok = r0 + kk, b = tok / p.N, nn = tok - b * p.N;
+      return load_index_f(p.pos, p.pos_dtype, p.pbase + b * p.psb + nn * p.psn + (lane >> 4) * p.psc);
+    };
+    float pnext = load_pos(warp - 1);
     for (int64_t k = warp - 1; k < n; k += NW) {
+      const float pos = pnext;
+      pnext = load_pos(k + NW);
       const int s = int(k % rc.nslot);
       const uint32_t u = uint32_t(k / rc.nslot);
       if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
@@ -477,8 +486,6 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) { c[i] = __ldg(cp + i); sn[i] = -__ldg(sp + i); }
       } else {
-        const float pos = load_index_f(p.pos, p.pos_dtype,
-                                       p.pbase + b * p.psb + nn * p.psn + (lane >> 4) * p.psc);
         float sv, cv;
         sincos_t<T>(__fmul_rn(pos, invf), &sv, &cv);
 #pragma unroll
@@ -933,7 +940,25 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
                            : 0.f;
     }
     const int64_t nvec = int64_t(p.H) * (p.D / EPL);
+    // This lane's coordinates of the warp's next token are loaded one token
+    // ahead, so their latency overlaps the current token's work.
+    float cnext[NP];
+    auto load_coords = [&](int64_t kk, float (&cv)[NP]) {
+#pragma unroll
+      for (int q = 0; q < NP; ++q) cv[q] = 0.f;
+      if (p.use_table || kk >= n) return;
+      const int64_t tok = r0 + kk, l = tok - (tok / p.L) * p.L;
+#pragma unroll
+      for (int q = 0; q < NP; ++q)
+        if (axis[q] >= 0)
+          cv[q] = load_index_f(p.coords, p.coord_dtype, p.cbase + l * p.csl + axis[q] * p.csa);
+    };
+    load_coords(warp - 1, cnext);
     for (int64_t k = warp - 1; k < n; k += NW) {
+      float ccur[NP];
+#pragma unroll
+      for (int q = 0; q < NP; ++q) ccur[q] = cnext[q];
+      load_coords(k + NW, cnext);
       const int s = int(k % rc.nslot);
       const uint32_t u = uint32_t(k / rc.nslot);
       if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
@@ -959,8 +984,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
           if (axis[q] >= 0) {
-            const float cv = load_index_f(p.coords, p.coord_dtype, p.cbase + l * p.csl + axis[q] * p.csa);
-            sincos_t<T>(__fmul_rn(cv, fr[q]), &sn[q], &cs[q]);
+            sincos_t<T>(__fmul_rn(ccur[q], fr[q]), &sn[q], &cs[q]);
           } else {
             cs[q] = 1.f;
             sn[q] = 0.f;

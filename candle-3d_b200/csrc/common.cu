@@ -161,9 +161,7 @@ extern "C" const char* l3d_last_error(void) { return l3d::g_last_error.c_str(); 
 extern "C" int l3d_kernel_status(int* status, int reset) {
   using namespace l3d;
   if (!status) return fail(L3D_E_NULL, "l3d_kernel_status: status is required");
-  int a = 0, b = 0;
-  if (norm_status_read(&a, reset) != cudaSuccess || rope_status_read(&b, reset) != cudaSuccess)
-    return fail(L3D_E_CUDA, "l3d_kernel_status: cannot read the status words");
-  *status = a ? a : b;
+  if (norm_status_read(status, reset) != cudaSuccess)
+    return fail(L3D_E_CUDA, "l3d_kernel_status: cannot read the status word");
   return L3D_OK;
 }

@@ -39,10 +39,9 @@ int sm_count();
 // context, so a process that drives several GPUs sets it on each.  Returns
 // the result of the first attempt on this device.
 cudaError_t set_smem_limit(const void* kernel, int bytes);
-// Per-device status words of the kernels that take no workspace (row-norm
-// and 3D RoPE ring kernels): copy to *status, clear when reset != 0.
+// Per-device status word of the kernels that take no workspace (the
+// row-norm ring kernel): copy to *status, clear when reset != 0.
 cudaError_t norm_status_read(int* status, int reset);
-cudaError_t rope_status_read(int* status, int reset);
 
 // Byte address of the first element of a view.
 inline const char* elem_ptr(const l3d_tensor* t) {

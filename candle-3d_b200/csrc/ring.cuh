@@ -1,6 +1,5 @@
 // Shared-memory ring of bulk-copied rows: the mbarrier helpers of the
-// row kernels that stream whole rows through shared memory (row-norm, 3D
-// RoPE).  A producer issues one cp.async.bulk per row into a slot and the
+// kernels that stream whole rows through shared memory (the row-norm ring).  A producer issues one cp.async.bulk per row into a slot and the
 // slot's `full` barrier completes when the bytes land; the consumer warp
 // arrives on the slot's `empty` barrier once it holds the row in registers.
 #pragma once

@@ -20,17 +20,8 @@
 #include <type_traits>
 
 #include "common.cuh"
-#include "ring.cuh"
 
 namespace l3d {
-
-// Ring kernels (rope2d_ring_kernel, rope3d_ring_kernel): the per-device
-// status word of their bounded waits and their shared-memory geometry.
-__device__ int g_rope_status;
-constexpr int kRopeRingProducers = 8;
-constexpr int kRopeRingMaxSlots = 96;
-constexpr size_t kRopeRingSmem = 200 * 1024;
-constexpr int64_t kRopeRingMinRows = 4096;
 
 // --------------------------------------------------------------------- helpers
 __device__ __forceinline__ float inv_freq_f32(float theta, float num, float den) {
@@ -354,220 +345,6 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope2d_kernel(con
   }
 }
 
-// ----------------------------------------------------------- ring variant
-// q (and k) with a token's heads contiguous (head stride 64, e.g. views of a
-// [B, N, 3, H, 64] projection or of [T, C] rows) and at least 4096 tokens:
-// one CTA per SM streams its block of tokens through shared-memory slots
-// (one bulk copy per tensor row, eight producer lanes); each consumer warp
-// copies its token's chunks (the rope2d_kernel lane layout) into registers,
-// releases the slot and applies rope2d_chunks (identical bits).  Bounded
-// waits; on expiry status 5 goes to g_rope_status and the block drains its
-// copies.
-struct Rope2dRingCfg {
-  int nslot;            // multiple of kRopeRingProducers
-  uint32_t row_bytes;   // H * 64 * element size (one tensor)
-  uint32_t slot_bytes;  // ntensor * row_bytes
-  uint64_t wait_ns;
-};
-
-template <typename T, int NIT, int NW>
-__global__ void __launch_bounds__(32 * (NW + 1), 1)
-    rope2d_ring_kernel(const Rope2dParams p, const Rope2dRingCfg rc) {
-  extern __shared__ __align__(128) unsigned char rsm2[];
-  __shared__ __align__(16) float aff[2][2][64];
-  unsigned char* slots = rsm2;
-  uint64_t* full = reinterpret_cast<uint64_t*>(slots + size_t(rc.nslot) * rc.slot_bytes);
-  uint64_t* empty = full + rc.nslot;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + rc.nslot);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = lane & 7, hg = lane >> 3;
-  const int ea = 32 * (j >> 2) + 4 * (j & 3);
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < rc.nslot; ++s) {
-      ring_bar_init(&full[s], 1);
-      ring_bar_init(&empty[s], 1);
-    }
-    *abort_flag = 0;
-    ring_init_fence();
-  }
-  __syncthreads();
-  const int64_t tokens = p.B * p.N;
-  const int64_t per = (tokens + gridDim.x - 1) / gridDim.x;
-  const int64_t r0 = int64_t(blockIdx.x) * per;
-  const int64_t n = r0 < tokens ? (tokens - r0 < per ? tokens - r0 : per) : 0;
-  int64_t last = -1;
-  auto issue = [&](int64_t k) {
-    const int s = int(k % rc.nslot);
-    const int64_t tok = r0 + k, b = tok / p.N, nn = tok - b * p.N;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
-                     smem_addr(&full[s])),
-                 "r"(rc.slot_bytes)
-                 : "memory");
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      if (t >= p.ntensor) break;
-      const HeadView& iv = p.in[t];
-      const T* src = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + nn * iv.sn;
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-              "r"(smem_addr(slots + size_t(s) * rc.slot_bytes + size_t(t) * rc.row_bytes)),
-          "l"(src), "r"(rc.row_bytes), "r"(smem_addr(&full[s]))
-          : "memory");
-    }
-    last = k;
-  };
-  const int64_t first = n < rc.nslot ? n : rc.nslot;
-  if (warp == 0 && lane < kRopeRingProducers)
-    for (int64_t k = lane; k < first; k += kRopeRingProducers) issue(k);
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    const int t = i >> 7, wb = (i >> 6) & 1, e = i & 63;
-    float v = wb ? 0.f : 1.f;
-    if (t < p.ntensor && p.do_norm) {
-      const ChanVec& cv = wb ? p.b[t] : p.w[t];
-      if (cv.ptr) {
-        float one[1];
-        load_chan<1>(cv, 0, e, one);
-        v = one[0];
-      }
-    }
-    aff[t][wb][e] = v;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    if (lane < kRopeRingProducers) {
-      int64_t k = lane;
-      while (k < first) k += kRopeRingProducers;
-      for (; k < n && !*abort_flag; k += kRopeRingProducers) {
-        const int s = int(k % rc.nslot);
-        const uint32_t u = uint32_t(k / rc.nslot);
-        if (!ring_wait(&empty[s], (u - 1) & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
-        issue(k);
-      }
-    }
-  } else {
-    const float invf = inv_freq_f32(p.theta, float(2 * (lane & 15)), 32.0f);
-    using R = typename Raw4<T>::type;
-    // This lane's position of the warp's next token, loaded one token ahead.
-    auto load_pos = [&](int64_t kk) {
-      if (p.use_table || kk >= n) return 0.f;
-      const int64_t tok = r0 + kk, b = tok / p.N, nn = tok - b * p.N;
-      return load_index_f(p.pos, p.pos_dtype, p.pbase + b * p.psb + nn * p.psn + (lane >> 4) * p.psc);
-    };
-    float pnext = load_pos(warp - 1);
-    for (int64_t k = warp - 1; k < n; k += NW) {
-      const float pos = pnext;
-      pnext = load_pos(k + NW);
-      const int s = int(k % rc.nslot);
-      const uint32_t u = uint32_t(k / rc.nslot);
-      if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
-      R ra[2][NIT], rb[2][NIT];
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const T* row = reinterpret_cast<const T*>(slots + size_t(s) * rc.slot_bytes +
-                                                  size_t(t) * rc.row_bytes);
-#pragma unroll
-        for (int it = 0; it < NIT; ++it) {
-          const int h = 4 * it + hg;
-          if (t < p.ntensor && h < p.H) {
-            ra[t][it] = *reinterpret_cast<const R*>(row + h * 64 + ea);
-            rb[t][it] = *reinterpret_cast<const R*>(row + h * 64 + ea + 16);
-          } else {
-            ra[t][it] = rb[t][it] = R{};
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) ring_arrive(&empty[s]);
-      const int64_t tok = r0 + k, b = tok / p.N, nn = tok - b * p.N;
-      float c[4], sn[4];
-      if (p.use_table) {
-        const float* cp = p.cosp + p.cbase + b * p.csb + nn * p.csn + ea;
-        const float* sp = p.sinp + p.sbase + b * p.ssb + nn * p.ssn + ea;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) { c[i] = __ldg(cp + i); sn[i] = -__ldg(sp + i); }
-      } else {
-        float sv, cv;
-        sincos_t<T>(__fmul_rn(pos, invf), &sv, &cv);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          c[i] = __shfl_sync(0xffffffffu, cv, 4 * j + i);
-          sn[i] = __shfl_sync(0xffffffffu, sv, 4 * j + i);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        if (t >= p.ntensor) break;
-        const HeadView& ov = p.out[t];
-        T* dst0 = static_cast<T*>(ov.data) + ov.base + b * ov.sb + nn * ov.sn + ea;
-        Rope2dCoef kc;
-        rope2d_coef(aff[t], ea, c, sn, kc);
-#pragma unroll
-        for (int it = 0; it < NIT; ++it) {
-          if (4 * it >= p.H) break;  // warp-uniform
-          const int h = 4 * it + hg;
-          float2 oa[2], ob[2];
-          rope2d_chunks<T>(ra[t][it], rb[t][it], kc, p.do_norm, p.eps, oa, ob);
-          if (h < p.H) {
-            T* dst = dst0 + int64_t(h) * ov.sh;
-            store4x2<T>(dst, oa);
-            store4x2<T>(dst + 16, ob);
-          }
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (*abort_flag && warp == 0 && lane < kRopeRingProducers && last >= 0) {
-    for (int s = lane; s < rc.nslot; s += kRopeRingProducers) {
-      if (last < s) continue;
-      const int64_t ks = last - ((last - s) % rc.nslot);
-      ring_wait(&full[s], uint32_t(ks / rc.nslot) & 1u, abort_flag, rc.wait_ns, true, &g_rope_status);
-    }
-  }
-}
-
-template <typename T, int NIT, int NW>
-static int launch_rope2d_ring(const Rope2dParams& p, const Rope2dRingCfg& rc, size_t smem,
-                              cudaStream_t s) {
-  auto k = rope2d_ring_kernel<T, NIT, NW>;
-  // The limit is set once per device to the most any launch of it uses.
-  if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRopeRingSmem)) != cudaSuccess) return -1;
-  int64_t grid = (p.B * p.N + NW - 1) / NW;
-  if (grid > sm_count()) grid = sm_count();
-  k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);
-  return 0;
-}
-
-// 1: launched; 0: outside the ring kernel's envelope; -1: CUDA error.
-template <typename T>
-static int try_rope2d_ring(const Rope2dParams& p, cudaStream_t s) {
-  if (p.B * p.N < kRopeRingMinRows || p.H > 32) return 0;
-  for (int t = 0; t < p.ntensor; ++t)
-    if (p.H > 1 && p.in[t].sh != 64) return 0;
-  const uint32_t row_bytes = uint32_t(p.H) * 64u * uint32_t(sizeof(T));
-  Rope2dRingCfg rc{};
-  rc.row_bytes = row_bytes;
-  rc.slot_bytes = row_bytes * uint32_t(p.ntensor);
-  if (rc.slot_bytes > 8192) return 0;
-  const size_t bar_bytes = size_t(2) * kRopeRingMaxSlots * 8 + 16;
-  int64_t ns = int64_t((kRopeRingSmem - bar_bytes) / rc.slot_bytes);
-  if (ns > kRopeRingMaxSlots) ns = kRopeRingMaxSlots;
-  ns -= ns % kRopeRingProducers;
-  if (ns < 2 * kRopeRingProducers) return 0;
-  rc.nslot = int(ns);
-  rc.wait_ns = 2000000000ull;
-  const size_t smem = size_t(rc.nslot) * rc.slot_bytes + size_t(2) * rc.nslot * 8 + 16;
-  int r;
-  if constexpr (sizeof(T) == 4) {
-    if (p.H <= 16) r = launch_rope2d_ring<T, 4, 12>(p, rc, smem, s);
-    else r = launch_rope2d_ring<T, 8, 8>(p, rc, smem, s);
-  } else {
-    if (p.H <= 16) r = launch_rope2d_ring<T, 4, 16>(p, rc, smem, s);
-    else r = launch_rope2d_ring<T, 8, 12>(p, rc, smem, s);
-  }
-  return r == 0 ? 1 : -1;
-}
-
 __global__ void rope2d_tables_kernel(int64_t B, int64_t N, const void* pos, int pos_dtype,
                                      int64_t pbase, int64_t psb, int64_t psn, int64_t psc,
                                      float theta, int D, float* cosp, float* sinp) {
@@ -856,213 +633,6 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope3d_kernel(con
   }
 }
 
-// ----------------------------------------------------------- ring variant
-// 16-bit activations with D = 128 and the heads of a token contiguous (a row
-// of H * 128 elements, e.g. the bench's [T, C] rows or a [B, L, H, D] q/k):
-// one CTA per SM streams its block of tokens through a ring of shared-memory
-// slots filled by bulk copies (one per token row, eight producer lanes),
-// consumer warps take every NW-th token, copy its row into registers,
-// release the slot and apply the same per-chunk arithmetic as rope3d_kernel
-// (rope3d_pk_chunk), so the two give identical bits.  Bounded waits; on expiry
-// status 5 goes to g_rope_status and the block drains its copies.
-
-struct RopeRingCfg {
-  int nslot;            // multiple of kRopeRingProducers
-  uint32_t row_bytes;   // H * D * 2
-  size_t g_bytes;       // staged gamma, 128-aligned
-  uint64_t wait_ns;
-};
-
-template <typename T, int NV, int NW>
-__global__ void __launch_bounds__(32 * (NW + 1), 1)
-    rope3d_ring_kernel(const Rope3dParams p, const RopeRingCfg rc) {
-  constexpr int LPH = 16, EPL = 8, NP = 4;
-  extern __shared__ __align__(128) unsigned char rsm[];
-  float* gsm = reinterpret_cast<float*>(rsm);  // [H, D] gamma * sqrt(D), de-interleaved
-  unsigned char* slots = rsm + rc.g_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(slots + size_t(rc.nslot) * rc.row_bytes);
-  uint64_t* empty = full + rc.nslot;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + rc.nslot);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = lane % LPH, hg = lane / LPH;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < rc.nslot; ++s) {
-      ring_bar_init(&full[s], 1);
-      ring_bar_init(&empty[s], 1);
-    }
-    *abort_flag = 0;
-    ring_init_fence();
-  }
-  __syncthreads();
-  const int64_t tokens = p.B * p.L;
-  const int64_t per = (tokens + gridDim.x - 1) / gridDim.x;
-  const int64_t r0 = int64_t(blockIdx.x) * per;
-  const int64_t n = r0 < tokens ? (tokens - r0 < per ? tokens - r0 : per) : 0;
-  int64_t last = -1;
-  auto issue = [&](int64_t k) {
-    const int s = int(k % rc.nslot);
-    const int64_t tok = r0 + k, b = tok / p.L, l = tok - b * p.L;
-    ring_load(slots + size_t(s) * rc.row_bytes,
-              static_cast<const T*>(p.x) + p.xbase + b * p.xsb + l * p.xsl, rc.row_bytes, &full[s]);
-    last = k;
-  };
-  const int64_t first = n < rc.nslot ? n : rc.nslot;
-  if (warp == 0 && lane < kRopeRingProducers)
-    for (int64_t k = lane; k < first; k += kRopeRingProducers) issue(k);
-  if (p.gamma) {
-    for (int i = threadIdx.x; i < p.H * p.D; i += blockDim.x) {
-      const int h = i / p.D, d = i - h * p.D;
-      gsm[h * p.D + (d & ~3) + ((d & 1) << 1) + ((d >> 1) & 1)] = p.gamma[int64_t(h) * p.gsh + d] * p.scale;
-    }
-  }
-  __syncthreads();
-  const int half = p.D / 2;
-  if (warp == 0) {
-    if (lane < kRopeRingProducers) {
-      int64_t k = lane;
-      while (k < first) k += kRopeRingProducers;
-      for (; k < n && !*abort_flag; k += kRopeRingProducers) {
-        const int s = int(k % rc.nslot);
-        const uint32_t u = uint32_t(k / rc.nslot);
-        if (!ring_wait(&empty[s], (u - 1) & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
-        issue(k);
-      }
-    }
-  } else {
-    float fr[NP];
-    int axis[NP];
-#pragma unroll
-    for (int k = 0; k < NP; ++k) {
-      const int pr = m * NP + k;
-      const int a = p.freq_dim > 0 ? pr / p.freq_dim : 3;
-      axis[k] = (p.coords && pr < half && a < 3) ? a : -1;
-      fr[k] = axis[k] >= 0 ? inv_freq_f32(p.theta, float(pr - a * p.freq_dim), float(p.freq_dim))
-                           : 0.f;
-    }
-    const int64_t nvec = int64_t(p.H) * (p.D / EPL);
-    // This lane's coordinates of the warp's next token are loaded one token
-    // ahead, so their latency overlaps the current token's work.
-    float cnext[NP];
-    auto load_coords = [&](int64_t kk, float (&cv)[NP]) {
-#pragma unroll
-      for (int q = 0; q < NP; ++q) cv[q] = 0.f;
-      if (p.use_table || kk >= n) return;
-      const int64_t tok = r0 + kk, l = tok - (tok / p.L) * p.L;
-#pragma unroll
-      for (int q = 0; q < NP; ++q)
-        if (axis[q] >= 0)
-          cv[q] = load_index_f(p.coords, p.coord_dtype, p.cbase + l * p.csl + axis[q] * p.csa);
-    };
-    load_coords(warp - 1, cnext);
-    for (int64_t k = warp - 1; k < n; k += NW) {
-      float ccur[NP];
-#pragma unroll
-      for (int q = 0; q < NP; ++q) ccur[q] = cnext[q];
-      load_coords(k + NW, cnext);
-      const int s = int(k % rc.nslot);
-      const uint32_t u = uint32_t(k / rc.nslot);
-      if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_rope_status)) break;
-      const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(s) * rc.row_bytes);
-      uint4 v[NV];
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int64_t vi = lane + 32 * i;
-        v[i] = vi < nvec ? src[vi] : make_uint4(0, 0, 0, 0);
-      }
-      __syncwarp();
-      if (lane == 0) ring_arrive(&empty[s]);
-      const int64_t tok = r0 + k, b = tok / p.L, l = tok - b * p.L;
-      float cs[NP], sn[NP];
-      if (p.use_table) {
-#pragma unroll
-        for (int q = 0; q < NP; ++q) {
-          const int pr = m * NP + q;
-          cs[q] = pr < half ? __ldg(p.cost + p.tcbase + l * p.tcsl + pr) : 1.f;
-          sn[q] = pr < half ? __ldg(p.sint + p.tsbase + l * p.tssl + pr) : 0.f;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < NP; ++q) {
-          if (axis[q] >= 0) {
-            sincos_t<T>(__fmul_rn(ccur[q], fr[q]), &sn[q], &cs[q]);
-          } else {
-            cs[q] = 1.f;
-            sn[q] = 0.f;
-          }
-        }
-      }
-      T* yt = static_cast<T*>(p.y) + p.ybase + b * p.ysb + l * p.ysl + m * EPL;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        if (2 * i >= p.H) break;  // warp-uniform
-        const int h = 2 * i + hg;
-        const bool valid = h < p.H;
-        const uint4 o = rope3d_pk_chunk<T, LPH>(v[i], cs, sn,
-                                                p.gamma ? gsm + h * p.D + m * EPL : nullptr, valid);
-        if (valid) st_act_raw(reinterpret_cast<uint4*>(yt + int64_t(h) * p.D), o);
-      }
-    }
-  }
-  __syncthreads();
-  if (*abort_flag && warp == 0 && lane < kRopeRingProducers && last >= 0) {
-    for (int s = lane; s < rc.nslot; s += kRopeRingProducers) {
-      if (last < s) continue;
-      const int64_t ks = last - ((last - s) % rc.nslot);
-      ring_wait(&full[s], uint32_t(ks / rc.nslot) & 1u, abort_flag, rc.wait_ns, true, &g_rope_status);
-    }
-  }
-}
-
-template <typename T, int NV, int NW>
-static int launch_rope3d_ring(const Rope3dParams& p, const RopeRingCfg& rc, size_t smem,
-                              cudaStream_t s) {
-  auto k = rope3d_ring_kernel<T, NV, NW>;
-  // The limit is set once per device to the most any launch of it uses.
-  if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRopeRingSmem)) != cudaSuccess) return -1;
-  int64_t grid = (p.B * p.L + NW - 1) / NW;
-  if (grid > sm_count()) grid = sm_count();
-  k<<<dim3(unsigned(grid)), 32 * (NW + 1), smem, s>>>(p, rc);
-  return 0;
-}
-
-// 1: launched; 0: outside the ring kernel's envelope; -1: CUDA error.
-template <typename T>
-static int try_rope3d_ring(const Rope3dParams& p, cudaStream_t s) {
-  if constexpr (sizeof(T) != 2) {
-    return 0;
-  } else {
-    if (p.D != 128 || p.xsh != p.D || p.ysh != p.D || p.B * p.L < kRopeRingMinRows) return 0;
-    const uint32_t row_bytes = uint32_t(p.H) * 128u * 2u;
-    if (p.H < 1 || row_bytes > 8192) return 0;
-    RopeRingCfg rc{};
-    rc.row_bytes = row_bytes;
-    rc.g_bytes = p.gamma ? ((size_t(p.H) * 128 * 4 + 127) & ~size_t(127)) : 0;
-    const size_t bar_bytes = size_t(2) * kRopeRingMaxSlots * 8 + 16;
-    int64_t ns = int64_t((kRopeRingSmem - rc.g_bytes - bar_bytes) / row_bytes);
-    if (ns > kRopeRingMaxSlots) ns = kRopeRingMaxSlots;
-    ns -= ns % kRopeRingProducers;
-    if (ns < 2 * kRopeRingProducers) return 0;
-    rc.nslot = int(ns);
-    rc.wait_ns = 2000000000ull;
-    const size_t smem = rc.g_bytes + size_t(rc.nslot) * row_bytes + size_t(2) * rc.nslot * 8 + 16;
-    const int nv = (p.H + 1) / 2;
-    int r;
-    if (nv <= 4) r = launch_rope3d_ring<T, 4, 24>(p, rc, smem, s);
-    else if (nv <= 8) r = launch_rope3d_ring<T, 8, 24>(p, rc, smem, s);
-    else r = launch_rope3d_ring<T, 16, 16>(p, rc, smem, s);
-    return r == 0 ? 1 : -1;
-  }
-}
-
-cudaError_t rope_status_read(int* status, int reset) {
-  cudaError_t e = cudaMemcpyFromSymbol(status, g_rope_status, sizeof(int));
-  if (e == cudaSuccess && reset) {
-    const int zero = 0;
-    e = cudaMemcpyToSymbol(g_rope_status, &zero, sizeof(int));
-  }
-  return e;
-}
-
 __global__ void rope3d_tables_kernel(int64_t L, const void* coords, int cdt, int64_t cbase,
                                      int64_t csl, int64_t csa, int half, int fd, float theta,
                                      float* cosp, float* sinp) {
@@ -1196,13 +766,8 @@ static int run_rope2d(const l3d_tensor* const* xs, const l3d_tensor* const* ws,
     p.cosp = static_cast<const float*>(cosf_t->data);
     p.sinp = static_cast<const float*>(sinf_t->data);
   }
-  int ring = 0;
-  L3D_DISPATCH_FLOAT(dt, T, { ring = try_rope2d_ring<T>(p, stream); });
-  if (ring < 0) return fail(L3D_E_CUDA, "%s: cannot reserve the ring kernel's shared memory", op);
-  if (!ring) {
-    const int blocks = launch_grid_warps(p.B * p.N);
-    L3D_DISPATCH_FLOAT(dt, T, { rope2d_kernel<T><<<blocks, 256, 0, stream>>>(p); });
-  }
+  const int blocks = launch_grid_warps(p.B * p.N);
+  L3D_DISPATCH_FLOAT(dt, T, { rope2d_kernel<T><<<blocks, 256, 0, stream>>>(p); });
   return check_launch(op);
 }
 
@@ -1341,13 +906,7 @@ static int run_rope3d(const l3d_tensor* x, const l3d_tensor* gamma, const l3d_te
   const size_t smem = p.gamma ? size_t(p.H) * size_t(p.D) * sizeof(float) : 0;
   if (smem > 48 * 1024) return fail(L3D_E_UNSUPPORTED, "%s: gamma [H, D] above 12288 values", op);
   const int blocks = launch_grid_warps(p.B * p.L);
-  int ring = 0;
   if (fast) {
-    L3D_DISPATCH_FLOAT(x->dtype, T, { ring = try_rope3d_ring<T>(p, stream); });
-    if (ring < 0) return fail(L3D_E_CUDA, "%s: cannot reserve the ring kernel's shared memory", op);
-  }
-  if (ring) {
-  } else if (fast) {
     const int lph = p.D / 8 <= 4 ? 4 : p.D / 8 <= 8 ? 8 : p.D / 8 <= 16 ? 16 : 32;
     L3D_DISPATCH_FLOAT(x->dtype, T, {
       switch (lph) {

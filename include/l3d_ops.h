@@ -100,8 +100,8 @@ int l3d_layer_norm(const l3d_tensor* x, const l3d_tensor* weight, const l3d_tens
 
 /* Status of the kernels that take no workspace, on the current device (no
  * counterpart in the reference: Candle ops report errors only on the host).
- * The row-norm and 3D RoPE entries stream long inputs through shared memory
- * with bounded waits; a wait that runs out (status 5) is recorded in a
+ * The row-norm entries stream long inputs through shared memory with bounded
+ * waits; a wait that runs out (status 5) is recorded in a
  * per-device word, since these entries have no workspace to hold a status.
  * This call copies it to *status (synchronising with the device) and clears
  * it when reset != 0.  0 = no wait has expired. */

@@ -15,7 +15,9 @@ the timed output against the CPU oracle.
 
 The same line carries the metric's other half, `block_stack`: tokens/s of ONE
 VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
-head-parallel), and at N = 1 `config1_fp32`, the f32 micro-suite per op.
+head-parallel), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
+`chain_c1024`, the chain at C = 1024 (its middle kernel is the VGGT per-head
+LN + 2D RoPE).
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Multi-GPU: launched by torch.distributed.run, one rank per GPU; every rank
@@ -394,6 +396,42 @@ def time_cpu_chain(orc, C, rows, seed, min_seconds=10.0):
         if el >= min_seconds:
             break
     return 12.0 * rows * C * n / el / 1e9, n, el
+
+
+# ------------------------------------------------ a second chain width
+def chain_width_record(ops, dev, T, C, steps, warmup):
+    """The config-5 chain at another width on one GPU (C = 1024 swaps in the
+    VGGT per-head LN + 2D RoPE kernel, a5): per-kernel CUDA-event times of
+    `steps` launches after `warmup`, algorithmic GB/s (4 B per element per
+    kernel) and fraction of the measured HBM peak."""
+    import torch
+
+    peak, peak_kind = measured_peaks()
+    chain = Chain(ops, make_inputs(T, C, 20261201, dev), T, C)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(warmup, 3)):
+        chain.step()
+    torch.cuda.synchronize()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(3)] for _ in range(steps)]
+    for st in range(steps):
+        for i in range(3):
+            evs[st][i][0].record(stream)
+            chain.op(i)
+            evs[st][i][1].record(stream)
+    torch.cuda.synchronize()
+    rec = {"workload": f"chain at C={C}, {T} rows, bf16", "peak": peak, "peak_source": peak_kind,
+           "kernels": {}}
+    tot = 0.0
+    for i, name in enumerate(chain.names):
+        ms = sum(evs[st][i][0].elapsed_time(evs[st][i][1]) for st in range(steps)) / steps
+        tot += ms
+        gbs = 4.0 * T * C / (ms / 1e3) / 1e9
+        rec["kernels"][name] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    rec["chain_GBps"] = round(12.0 * T * C / (tot / 1e3) / 1e9, 1)
+    rec["launches"] = 3 * (steps + max(warmup, 3))
+    del chain
+    return rec
 
 
 # ----------------------------------------------------- config 1 (fp32 suite)
@@ -1281,7 +1319,10 @@ def main():
     # the N GPUs; and, at N = 1, config 1 (the f32 micro-suite)
     del chain, inp
     torch.cuda.empty_cache()
-    config1 = None
+    config1 = chain1024 = None
+    if rank == 0 and world == 1 and not args.no_config1 and C != 1024:
+        chain1024 = chain_width_record(ops, dev, T, 1024, args.steps, args.warmup)
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_config1:
         from oracle import oracle as orc
 
@@ -1313,6 +1354,7 @@ def main():
             "parity": parity,
             "block_stack": stack,
             "config1_fp32": config1,
+            "chain_c1024": chain1024,
         }
         print(json.dumps(line))
     if world > 1:

@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
 }
 
 // ------------------------------------------------------------ ring variant
-// Rows without a residual branch, long enough inputs: one CTA per SM streams
+// Rows of 2-8 KB without a residual branch, long inputs: one CTA per SM streams
 // its contiguous block of rows through a ring of shared-memory slots filled by
 // bulk copies (cp.async.bulk, one per row, issued by eight producer lanes of
 // warp 0, so up to `nslot` rows are in flight per SM without holding them in
@@ -681,8 +681,11 @@ static bool pick_geometry(int64_t nvec, bool scalar, int* G, int* NV) {
 }
 
 // Ring path selection (rowring_kernel): LN / RMS without a residual branch,
-// 16-byte vectors, rows of at most 8 KB, enough rows for every SM.
-constexpr int64_t kRingMinRows = 4096;
+// 16-byte vectors, rows of 2 to 8 KB, enough rows to keep every SM's ring
+// busy (shorter rows or inputs run faster in the register kernel, which
+// packs several rows per warp and fills the device sooner).
+constexpr int64_t kRingMinRows = 32768;
+constexpr uint32_t kRingMinRowBytes = 2048;
 
 template <typename T, int NV, int NW>
 static int launch_ring(const RowNormParams& p, const RingCfg& rc, size_t smem, cudaStream_t s) {
@@ -702,7 +705,8 @@ static int try_ring(const RowNormParams& p, cudaStream_t s) {
   const int es = int(sizeof(T));
   const int vec = 16 / es;
   const uint32_t row_bytes = uint32_t(p.C * es);
-  if (p.rows < kRingMinRows || row_bytes > 8192 || p.C % vec) return 0;
+  if (p.rows < kRingMinRows || row_bytes < kRingMinRowBytes || row_bytes > 8192 || p.C % vec)
+    return 0;
   const int64_t nv = (p.C / vec + 31) / 32;
   RingCfg rc{};
   rc.row_bytes = row_bytes;

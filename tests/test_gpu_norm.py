@@ -128,17 +128,17 @@ def test_empty_rows_are_noops(ops, dev):
 
 
 @pytest.mark.parametrize("dt", DTS)
-@pytest.mark.parametrize("C,affine", [(2048, False), (1536, True), (64, True), (4096, False)])
+@pytest.mark.parametrize("C,affine", [(2048, False), (1536, True), (1024, True), (4096, False)])
 def test_layer_norm_ring_path_rows(ops, orc, dev, dt, C, affine):
-    """Inputs of at least 4096 rows take the shared-memory ring kernel (bulk
-    copies of whole rows); rows of up to 8 KB, with and without affine
-    vectors, modulation and gate, and the kernels' status word stays 0."""
+    """Inputs of at least 32768 rows of 2-8 KB take the shared-memory ring
+    kernel (bulk copies of whole rows): with and without affine vectors,
+    modulation and gate; the kernels' status word stays 0."""
     import ctypes
 
     if C * {"f32": 4, "bf16": 2, "f16": 2}[dt] > 8192:
         C = 2048
     r = rng(7)
-    T = 5000
+    T = 32768 + 77
     x, xv = to_dev(r.standard_normal((T, C)), dt, dev)
     w = b = wv = bv = None
     if affine:
@@ -158,3 +158,18 @@ def test_layer_norm_ring_path_rows(ops, orc, dev, dt, C, affine):
     st = ctypes.c_int(-1)
     assert ops._lib.lib().l3d_kernel_status(ctypes.byref(st), 1) == 0
     assert st.value == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+def test_layer_norm_modulate_ring_per_batch_chunks(ops, orc, dev, dt):
+    """The ring kernel with per-batch adaLN vectors: shift / scale / gate as
+    chunk views of a [B, 6C] vector over 2 x 16400 rows of C = 1024."""
+    r = rng(8)
+    B, N, C = 2, 16400, 1024
+    x, xv = to_dev(r.standard_normal((B, N, C)), dt, dev)
+    mod, modv = to_dev(0.1 * r.standard_normal((B, 6 * C)), dt, dev)
+    sh, sc, gt, *_ = ops.chunk_modulation(mod)
+    y = ops.layer_norm_modulate(x, sh, sc, gate=gt, eps=1e-6)
+    ref = orc.layer_norm_modulate(xv, shift=modv[:, :C], scale=modv[:, C:2 * C],
+                                  gate=modv[:, 2 * C:3 * C], eps=1e-6)
+    assert_close(y.float().cpu().numpy(), ref, dt, "ring per-batch adaLN")

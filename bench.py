@@ -15,7 +15,8 @@ the timed output against the CPU oracle.
 
 The same line carries the metric's other half, `block_stack`: tokens/s of ONE
 VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
-head-parallel), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
+head-parallel), at N > 1 `block_stack_replicas` (one whole scene per GPU, the
+throughput form), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
 `chain_c1024`, the chain at C = 1024 (its middle kernel is the VGGT per-head
 LN + 2D RoPE).
 
@@ -542,7 +543,7 @@ def _seconds(fn):
 
 
 # ------------------------------------------------- config 2, one scene split
-def vggt_scene(args, world, rank, local, check=True):
+def vggt_scene(args, world, rank, local, check=True, replicas=False):
     """Config 2 (VGGT-1B aggregator): one scene of S = 8 views x 1374 tokens
     through patch embedding, 24 frame + 24 global blocks and the final
     all-gather of the block outputs, split across the `world` ranks (S / world
@@ -552,7 +553,9 @@ def vggt_scene(args, world, rank, local, check=True):
     achieved TFLOP/s per GPU against the sustained bf16 peak, end-to-end
     tokens/s (pixels in from pinned host memory, gathered tokens out), and at
     world > 1 the sharded-vs-single-GPU output difference (rank 0 reruns the
-    scene alone)."""
+    scene alone).  With `replicas`, every rank runs a whole scene of its own
+    instead (no communication) and the tokens of all N scenes are counted:
+    the throughput form of the same stack."""
     import torch
 
     import __graft_entry__ as graft
@@ -567,9 +570,9 @@ def vggt_scene(args, world, rank, local, check=True):
     N = 5 + ph * ph
     if S % world:
         return {"unavailable": f"{S} views do not split over {world} ranks"}
-    sl = S // world
-    v0 = rank * sl
-    split = shard.SceneSplit() if world > 1 else None
+    sl = S if replicas else S // world
+    v0 = 0 if replicas else rank * sl
+    split = shard.SceneSplit() if world > 1 and not replicas else None
     inp = vggt_inputs(dev, S)
     agg = blocks.VggtAggregator(depth=24, device=dev)
     special = torch.cat([inp["special"][:1], inp["special"][1:].expand(S - 1, 5, C)], 0)
@@ -631,17 +634,17 @@ def vggt_scene(args, world, rank, local, check=True):
     e1.record(stream)
     barrier()
     ms = maxr(e0.elapsed_time(e1)) / args.steps
-    tokens = S * N
+    tokens = S * N * (world if replicas else 1)
     flops = 24 * (2 * 24 * tokens * C * C + 4 * S * N * N * C + 4 * (S * N) ** 2 * C)
     peak_tf = 1395.8
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
         peak_tf = float(json.loads(pk.read_text()).get("bf16_tflops_sustained", peak_tf))
-    ach = flops / (ms / 1e3) / 1e12 / world
+    ach = flops / (ms / 1e3) / 1e12 / (1 if replicas else world)
     # End to end: this rank's views' pixels in from pinned host memory, the
     # gathered scene tokens back out, every step.
     hp = px.cpu().pin_memory()
-    hy = torch.empty((tokens, C), dtype=torch.bfloat16).pin_memory()
+    hy = torch.empty((S * N, C), dtype=torch.bfloat16).pin_memory()
     barrier()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
@@ -656,7 +659,9 @@ def vggt_scene(args, world, rank, local, check=True):
         "ms_per_step": round(ms, 3), "steps": args.steps,
         "workload": "config2 VGGT-1B aggregator, ONE scene: patch embed + 24 frame / 24 global "
                     "blocks + final all-gather, S=8 views x 1374 tokens, dim 1024, 16 heads",
-        "parallelism": (f"scene split over {world} GPUs: {sl} view(s) per rank, global blocks "
+        "parallelism": (f"{world} replicas: one whole scene per GPU, no communication"
+                        if replicas else
+                        f"scene split over {world} GPUs: {sl} view(s) per rank, global blocks "
                         f"head-parallel ({16 // world} heads per rank, 2 NCCL all-to-alls)")
                        if world > 1 else "single GPU",
         "attention": args.attention, "cuda_graph": graph is not None,
@@ -666,7 +671,7 @@ def vggt_scene(args, world, rank, local, check=True):
         "e2e": {"value": round(tokens / (ems / 1e3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(hp.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2)},
     }
-    if world > 1 and check:
+    if world > 1 and check and not replicas:
         # The same scene on rank 0 alone (no split) against the gathered split output.
         sharded = out.float()
         if rank == 0:
@@ -1328,6 +1333,10 @@ def main():
 
         config1 = config1_record(ops, dev, None if args.no_cpu else orc)
     stack = None if args.no_stack else vggt_scene(args, world, rank, local)
+    stack_rep = None
+    if not args.no_stack and world > 1:
+        torch.cuda.empty_cache()
+        stack_rep = vggt_scene(args, world, rank, local, replicas=True)
 
     if rank == 0:
         line = {
@@ -1353,6 +1362,7 @@ def main():
             "cpu_baseline": cpu,
             "parity": parity,
             "block_stack": stack,
+            "block_stack_replicas": stack_rep,
             "config1_fp32": config1,
             "chain_c1024": chain1024,
         }

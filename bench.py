@@ -59,6 +59,8 @@ def parse():
                     help="end-to-end steps (default: --steps)")
     ap.add_argument("--e2e-chunks", type=int, default=32,
                     help="row chunks of the end-to-end copy/compute pipeline")
+    ap.add_argument("--no-fused-gather", action="store_true",
+                    help="N > 1: skip the GELU-with-peer-stores gather")
     ap.add_argument("--gather-chunks", type=int, default=16,
                     help="N > 1: row chunks of the overlapped final all-gather")
     ap.add_argument("--no-e2e", action="store_true")
@@ -1283,6 +1285,36 @@ def main():
         gsteps = max(3, min(args.steps, 10))
         gms = timed(gather_only, gsteps)
         cgms = timed(chain_and_gather, gsteps)
+        # Fused: the GELU kernel stores its rows into block `rank` of every
+        # rank's gather buffer (CUDA IPC peer memory over NVLink), so the last
+        # op and the gather are one pass; checked bit for bit against NCCL.
+        fused = None
+        if not args.no_fused_gather:
+            peer = shard.PeerRows(T, C, torch.bfloat16, dev)
+            dests = [peer.dest(p) for p in range(world)]
+            dests = dests[rank:] + dests[:rank]  # the local copy first
+
+            def chain_fused():
+                chain.op(0)
+                chain.op(1)
+                ops.activation_scatter(chain.b, dests, "gelu_tanh")
+
+            chain_fused()
+            chain.op(2)  # the same GELU into chain.a, for the NCCL reference gather
+            torch.cuda.synchronize()
+            barrier()
+            dist.all_gather_into_tensor(gathered[:world * T], chain.a)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(gathered[:world * T], peer.local))
+            fms = timed(chain_fused, gsteps)
+            fused = {"method": "last kernel (GELU) stores every row to all N gather buffers "
+                               "(CUDA IPC peer memory, NVLink), one pass; no NCCL",
+                     "chain_plus_gather_ms": round(fms, 3),
+                     "value_with_gather": round(world * 12.0 * T * C / (fms / 1e3) / 1e9, 3),
+                     "matches_nccl_gather": same,
+                     "gpu_launches_per_step": 3}
+            peer.close()
+            del peer
         per_rank = nch * rc * C * 2
         ingress = (world - 1) * per_rank
         v_g = world * 12.0 * nch * rc * C / (cgms / 1e3) / 1e9
@@ -1298,6 +1330,7 @@ def main():
             "bound": "NVLink ingress: (N-1) x bytes_per_rank per step on every GPU "
                      "(770 GB/s measured peer copy per direction)",
             "ingress_floor_ms": round(ingress / 770e9 * 1e3, 3),
+            "fused": fused,
         }
         del gathered
 

@@ -116,6 +116,7 @@ _SIGS = {
                                  _S], C.c_int),
     "l3d_attention_workspace_size": ([C.c_int64, C.c_int64, C.c_int64, C.c_int64], C.c_size_t),
     "l3d_kernel_status": ([C.POINTER(C.c_int), C.c_int], C.c_int),
+    "l3d_activation_scatter": ([C.c_int, _P, _P, C.c_int, _S], C.c_int),
     "l3d_attention": ([_P, _P, _P, C.c_float, _P, C.c_void_p, C.c_size_t, _S], C.c_int),
     "l3d_attention_selftest_timeout": ([_P, _P, _P, C.c_float, _P, C.c_void_p, C.c_size_t,
                                         C.c_uint32, _S], C.c_int),

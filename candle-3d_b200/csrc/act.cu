@@ -69,6 +69,51 @@ __global__ void __launch_bounds__(256) act_rows_kernel(const T* __restrict__ x, 
   }
 }
 
+// Activation whose result goes to several outputs: the local one and the
+// gather buffers of other GPUs mapped into this process (peer memory), so
+// the last op of the chain and the final all-gather are one pass.  Each
+// thread keeps kUnroll vectors in flight; the stores of a vector go to the
+// outputs in an order rotated by the block index, so concurrent blocks
+// write to different peers.
+constexpr int kMaxScatter = 8;
+struct ScatterOut {
+  void* p[kMaxScatter];
+  int n;
+};
+
+template <typename T, int A>
+__global__ void __launch_bounds__(256) act_scatter_kernel(const T* __restrict__ x, ScatterOut out,
+                                                          int64_t nvec) {
+  constexpr int VEC = Vec16<T>::N;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int rot = int(blockIdx.x % unsigned(out.n));
+  for (; i < nvec; i += kUnroll * stride) {
+    uint4 w[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = i + u * stride;
+      float f[VEC];
+      if (v < nvec) {
+        load_act<T, VEC>(x + v * VEC, f);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) f[e] = act_t<A, (sizeof(T) == 2)>(f[e]);
+        w[u] = pack(f, T());
+      }
+    }
+    for (int k = 0; k < out.n; ++k) {
+      int o = k + rot;
+      if (o >= out.n) o -= out.n;
+      uint4* dst = static_cast<uint4*>(out.p[o]);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t v = i + u * stride;
+        if (v < nvec) st_act_raw(dst + v, w[u]);
+      }
+    }
+  }
+}
+
 static bool is_contiguous(const l3d_tensor* t) {
   int64_t st = 1;
   for (int i = t->ndim - 1; i >= 0; --i) {
@@ -161,3 +206,41 @@ extern "C" int l3d_geglu(const l3d_tensor* x, const l3d_tensor* y, l3d_stream s)
   return run_act<ACT_GELU_ERF, true>(x, y, "l3d_geglu", reinterpret_cast<cudaStream_t>(s));
 }
 
+extern "C" int l3d_activation_scatter(int act, const l3d_tensor* x, const l3d_tensor* outs,
+                                      int n_out, l3d_stream stream) {
+  const char* op = "l3d_activation_scatter";
+  if (!x || no_data(x) || !outs) return fail(L3D_E_NULL, "%s: x and outs are required", op);
+  if (n_out < 1 || n_out > kMaxScatter)
+    return fail(L3D_E_UNSUPPORTED, "%s: 1 to %d outputs", op, kMaxScatter);
+  if (act != ACT_SILU && act != ACT_GELU_ERF && act != ACT_GELU_TANH)
+    return fail(L3D_E_UNSUPPORTED, "%s: act must be 1 (SiLU), 2 (GELU-erf) or 3 (GELU-tanh)", op);
+  if (!is_float_dtype(x->dtype)) return fail(L3D_E_DTYPE, "%s: x must be F32/F16/BF16", op);
+  if (!is_contiguous(x)) return fail(L3D_E_ALIGN, "%s: x must be contiguous", op);
+  const int64_t n = numel(x);
+  const int vec = 16 / dtype_size(x->dtype);
+  if (n % vec || reinterpret_cast<uintptr_t>(elem_ptr(x)) % 16)
+    return fail(L3D_E_ALIGN, "%s: x must be 16-byte aligned with a multiple of 16 bytes", op);
+  ScatterOut so{};
+  so.n = n_out;
+  for (int k = 0; k < n_out; ++k) {
+    const l3d_tensor* o = &outs[k];
+    if (no_data(o)) return fail(L3D_E_NULL, "%s: output %d has no data", op, k);
+    if (o->dtype != x->dtype) return fail(L3D_E_DTYPE, "%s: output %d dtype differs", op, k);
+    if (numel(o) != n || !is_contiguous(o))
+      return fail(L3D_E_SHAPE, "%s: output %d must be contiguous with x's element count", op, k);
+    if (reinterpret_cast<uintptr_t>(elem_ptr(o)) % 16)
+      return fail(L3D_E_ALIGN, "%s: output %d must be 16-byte aligned", op, k);
+    so.p[k] = const_cast<char*>(elem_ptr(o));
+  }
+  if (n == 0) return L3D_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t nvec = n / vec;
+  L3D_DISPATCH_FLOAT(x->dtype, T, {
+    const T* xp = reinterpret_cast<const T*>(elem_ptr(x));
+    const int g = grid_for(nvec / kUnroll);
+    if (act == ACT_SILU) act_scatter_kernel<T, ACT_SILU><<<g, 256, 0, s>>>(xp, so, nvec);
+    else if (act == ACT_GELU_ERF) act_scatter_kernel<T, ACT_GELU_ERF><<<g, 256, 0, s>>>(xp, so, nvec);
+    else act_scatter_kernel<T, ACT_GELU_TANH><<<g, 256, 0, s>>>(xp, so, nvec);
+  });
+  return check_launch(op);
+}

@@ -457,6 +457,24 @@ class SparseConv3d:
         return out
 
 
+def activation_scatter(x, outs, act="gelu_tanh"):
+    """act(x) stored to every output in one pass (l3d_activation_scatter):
+    `outs` are (device pointer, element offset) pairs of contiguous buffers
+    with x's dtype and element count, on this GPU or another GPU's memory
+    mapped here (shard.PeerRows.dest) - the last op of a block fused with the
+    final all-gather of the block outputs."""
+    _check_cuda(x)
+    arr = (_lib.L3dTensor * len(outs))()
+    for d, (ptr, off) in zip(arr, outs):
+        d.data = ptr
+        d.dtype = _lib._TORCH_TO_L3D[x.dtype]
+        d.ndim = 1
+        d.dims[0] = x.numel()
+        d.strides[0] = 1
+        d.offset = off
+    call("l3d_activation_scatter", ACT[act], ref(desc(x)), arr, len(outs), _s(x))
+
+
 # Status-word workspaces of l3d_attention, one per (device, stream): calls on
 # different streams then never clear or overwrite each other's status.
 _ATTN_WS = {}

@@ -105,3 +105,70 @@ class SceneSplit:
         out = local.new_empty((self.world * local.shape[0],) + tuple(local.shape[1:]))
         dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
         return out
+
+
+# ------------------------------------------ gather buffers in peer memory
+class _CudaArray:
+    """Raw device memory described through __cuda_array_interface__."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape),
+                                         "typestr": typestr, "strides": None, "version": 3}
+
+
+class PeerRows:
+    """A [world * rows, C] gather buffer on every rank, each mapped into every
+    other rank's address space with CUDA IPC, so a kernel on rank r can store
+    its `rows` output rows straight into block r of every rank's buffer over
+    NVLink (`dest(p)` is that block on rank p).  Collective: every rank of
+    `group` constructs it together.  `close()` (also collective) unmaps and
+    frees."""
+
+    def __init__(self, rows: int, C: int, dtype, device, group=None):
+        from cuda.bindings import runtime as rt
+
+        self.rt = rt
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.C, self.dtype = rows, C, dtype
+        self.device = torch.device(device)
+        esize = torch.empty((), dtype=dtype).element_size()
+        self.nbytes = self.world * rows * C * esize
+
+        def ok(res):
+            err = res[0] if isinstance(res, tuple) else res
+            if int(err) != 0:
+                raise RuntimeError(f"CUDA runtime error {err}")
+            return res[1] if isinstance(res, tuple) and len(res) > 1 else None
+
+        self._ok = ok
+        ok(rt.cudaSetDevice(self.device.index))
+        self.base = ok(rt.cudaMalloc(self.nbytes))
+        handle = ok(rt.cudaIpcGetMemHandle(self.base))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.reserved), group=group)
+        self.ptrs = []
+        for p in range(self.world):
+            if p == self.rank:
+                self.ptrs.append(int(self.base))
+                continue
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = handles[p]
+            self.ptrs.append(int(ok(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))))
+        n16 = self.nbytes // 2
+        raw = torch.as_tensor(_CudaArray(self.base, (n16,), "<i2"), device=self.device)
+        self.local = raw.view(dtype).view(self.world * rows, C)  # this rank's gathered rows
+
+    def dest(self, p: int):
+        """(device pointer, element offset) of this rank's block in rank p's buffer."""
+        return self.ptrs[p], self.rank * self.rows * self.C
+
+    def close(self):
+        dist.barrier(group=self.group)
+        for p, ptr in enumerate(self.ptrs):
+            if p != self.rank:
+                self._ok(self.rt.cudaIpcCloseMemHandle(ptr))
+        dist.barrier(group=self.group)
+        self.local = None
+        self._ok(self.rt.cudaFree(self.base))

@@ -227,6 +227,20 @@ int l3d_silu(const l3d_tensor* x, const l3d_tensor* y, l3d_stream stream);
  * y = x[.., :F] * gelu_erf(x[.., F:]). */
 int l3d_geglu(const l3d_tensor* x, const l3d_tensor* y, l3d_stream stream);
 
+/* Activation with its result stored to several outputs in one pass: the last
+ * op of a block fused with the final all-gather of the block outputs across
+ * GPUs (no single counterpart in the reference, whose pipeline runs on one
+ * device: it composes `Tensor::gelu` / `gelu_erf` / `silu`,
+ * crate/runtime/trellis2_blocks.rs:558-561, crate/runtime/nn_blocks.rs:233,
+ * with the gather of the row shards).  act: 1 SiLU, 2 GELU-erf, 3 GELU-tanh
+ * (the arithmetic of l3d_silu / l3d_gelu_erf / l3d_gelu_tanh).  x and the
+ * n_out (1..8) outputs are contiguous, 16-byte aligned, same dtype and
+ * element count; an output may be another GPU's memory mapped into this
+ * process (CUDA IPC / peer access), which the kernel writes over NVLink.
+ * The caller orders the peers' later reads (e.g. a barrier after the kernel). */
+int l3d_activation_scatter(int act, const l3d_tensor* x, const l3d_tensor* outs, int n_out,
+                           l3d_stream stream);
+
 /* ---- a4/a11: timestep embedding and the small (per-step) linears ---------------- */
 
 /* Sinusoidal timestep table for t [B] (F32) -> out [B, dim] (F32/BF16/F16).

@@ -155,3 +155,15 @@ def test_interleaved_blocks_tile_the_rows():
         seen = sorted(r for c in range(chunks) for k in range(world)
                       for r in range(*shard.interleaved_block(c, world, k, rc)))
         assert seen == list(range(chunks * world * rc))
+
+
+def test_peer_rows_layout():
+    """PeerRows.dest: rank r's block starts at row r * rows of every buffer."""
+    import __graft_entry__ as g
+
+    g.load_package()
+    from candle3d_b200 import shard
+
+    pr = shard.PeerRows.__new__(shard.PeerRows)
+    pr.rank, pr.rows, pr.C, pr.ptrs = 2, 10, 4, [100, 200, 300]
+    assert pr.dest(0) == (100, 80) and pr.dest(2) == (300, 80)

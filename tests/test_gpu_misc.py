@@ -185,3 +185,21 @@ def test_invalid_shapes_raise(ops, pkg, dev):
     q = torch.randn(1, 2, 3, 48, device=dev)  # head dim must be 64
     with pytest.raises(pkg._lib.L3dError):
         ops.rope_fused(q, torch.ones(1, 1, 3, 48, device=dev), torch.ones(1, 1, 3, 48, device=dev))
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+@pytest.mark.parametrize("act", ["gelu_tanh", "gelu_erf", "silu"])
+def test_activation_scatter_matches_activation(ops, dev, dt, act):
+    """l3d_activation_scatter (the last op fused with the final gather) stores
+    exactly the bits of the plain activation to every output (here three
+    buffers on this GPU; across GPUs they are peer-mapped blocks)."""
+    import torch
+
+    x = torch.randn(3000, 1024, device=dev).to(getattr(torch, {"bf16": "bfloat16", "f32": "float32"}[dt]))
+    ref = {"gelu_tanh": ops.gelu, "gelu_erf": ops.gelu_erf, "silu": ops.silu}[act](x)
+    bufs = [torch.zeros(4 * x.numel(), dtype=x.dtype, device=dev) for _ in range(3)]
+    offs = [0, x.numel(), 3 * x.numel()]
+    ops.activation_scatter(x, [(b.data_ptr(), o) for b, o in zip(bufs, offs)], act)
+    torch.cuda.synchronize()
+    for b, o in zip(bufs, offs):
+        assert torch.equal(b[o:o + x.numel()].view_as(x), ref)

@@ -637,7 +637,7 @@ def vggt_scene(args, world, rank, local, check=True, replicas=False):
     barrier()
     ms = maxr(e0.elapsed_time(e1)) / args.steps
     tokens = S * N * (world if replicas else 1)
-    flops = 24 * (2 * 24 * tokens * C * C + 4 * S * N * N * C + 4 * (S * N) ** 2 * C)
+    flops = 24 * (2 * 24 * S * N * C * C + 4 * S * N * N * C + 4 * (S * N) ** 2 * C)  # one scene
     peak_tf = 1395.8
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():

@@ -422,7 +422,7 @@ constexpr size_t kRingSmem = 200 * 1024;  // coefficients + slots + barriers
 __device__ int g_norm_status;
 
 struct RingCfg {
-  int nslot;             // multiple of kRingProducers
+  int nslot;             // multiple of kRingProducers and of the consumer warps
   uint32_t row_bytes;    // C * element size (a multiple of 16)
   size_t coef_bytes;     // 128-aligned
   uint64_t wait_ns;
@@ -712,11 +712,18 @@ static int try_ring(const RowNormParams& p, cudaStream_t s) {
   rc.row_bytes = row_bytes;
   rc.coef_bytes = (size_t(p.nbatch) * size_t(p.C) * 4 * (p.g2.ptr ? 3 : 2) + 127) & ~size_t(127);
   if (rc.coef_bytes > 64 * 1024) return 0;
+  // Slot s belongs to consumer warp s % NW and to producer lane s % 8 (rows
+  // k go to slot k % nslot and warp k % NW), so nslot is a multiple of both.
+  // Each slot's owner then consumes its rows in order, so no wait on a slot
+  // barrier is ever more than one phase ahead of it: the parity of the phase
+  // waited for is never ambiguous.
+  const int nw = nv <= 8 ? 24 : 16;
+  const int64_t unit = nw == 24 ? 24 : 16;  // lcm(NW, kRingProducers)
   const size_t bar_bytes = size_t(2) * kRingMaxSlots * 8 + 16;
   int64_t ns = int64_t((kRingSmem - rc.coef_bytes - bar_bytes) / row_bytes);
   if (ns > kRingMaxSlots) ns = kRingMaxSlots;
-  ns -= ns % kRingProducers;
-  if (ns < 2 * kRingProducers) return 0;
+  ns -= ns % unit;
+  if (ns < unit) return 0;
   rc.nslot = int(ns);
   rc.wait_ns = 2000000000ull;
   const size_t smem = rc.coef_bytes + size_t(rc.nslot) * row_bytes + size_t(2) * rc.nslot * 8 + 16;
@@ -725,6 +732,7 @@ static int try_ring(const RowNormParams& p, cudaStream_t s) {
   else if (nv <= 4) rcode = launch_ring<T, 4, 24>(p, rc, smem, s);
   else if (nv <= 8) rcode = launch_ring<T, 8, 24>(p, rc, smem, s);
   else rcode = launch_ring<T, 16, 16>(p, rc, smem, s);
+  static_assert(kRingMaxSlots % 24 == 0 && kRingMaxSlots % 16 == 0, "slot ownership");
   return rcode == 0 ? 1 : -1;
 }
 

@@ -220,3 +220,40 @@ def test_neighbor_pairs_ascending_and_symmetric(orc):
     for k in range(27):
         assert np.all(np.diff(d[k, :c[k]]) > 0)
         assert c[k] == c[26 - k]  # delta and -delta pair the same voxel pairs
+
+
+# --------------------------------------------------------------- torch CPU
+# An implementation that is neither this build's nor the reference's: torch's
+# CPU kernels compute the same textbook formulas Candle's ops are defined by
+# (LayerNorm with biased variance, GELU tanh / erf, SiLU, RMSNorm).  These
+# cases check the oracle against them in f32; they do not pin Candle's own
+# rounding, which no reference test exposes.
+def test_oracle_matches_torch_cpu_layer_ops(orc):
+    import torch
+    import torch.nn.functional as F
+
+    r = np.random.default_rng(77)
+    x = r.standard_normal((4, 96, 1024)).astype(np.float32) * 3 + 0.5
+    w = (1 + 0.02 * r.standard_normal(1024)).astype(np.float32)
+    b = (0.02 * r.standard_normal(1024)).astype(np.float32)
+    tx = torch.from_numpy(x)
+    ref = F.layer_norm(tx, (1024,), torch.from_numpy(w), torch.from_numpy(b), 1e-6).numpy()
+    got = orc.layer_norm(x, w, b, 1e-6)
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)) < 1e-5
+    sc = (0.1 * r.standard_normal((4, 1024))).astype(np.float32)
+    sh = (0.1 * r.standard_normal((4, 1024))).astype(np.float32)
+    ln = F.layer_norm(tx, (1024,), eps=1e-6)
+    ref = (ln * (1 + torch.from_numpy(sc)[:, None]) + torch.from_numpy(sh)[:, None]).numpy()
+    got = orc.layer_norm_modulate(x, shift=sh, scale=sc, eps=1e-6)
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)) < 1e-5
+    for name, fn in (("gelu_tanh", lambda t: F.gelu(t, approximate="tanh")),
+                     ("gelu_erf", F.gelu), ("silu", F.silu)):
+        ref = fn(tx).numpy()
+        got = getattr(orc, name)(x)
+        assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)) < 1e-5, name
+    q = r.standard_normal((2, 16, 50, 128)).astype(np.float32)
+    wq = (1 + 0.05 * r.standard_normal(128)).astype(np.float32)
+    tq = torch.from_numpy(q)
+    ref = (tq * torch.rsqrt(tq.pow(2).mean(-1, keepdim=True) + 1e-6) * torch.from_numpy(wq)).numpy()
+    got = orc.rms_norm_heads(q, wq, 1e-6)
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)) < 1e-5

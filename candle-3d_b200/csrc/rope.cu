@@ -281,9 +281,29 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope2d_kernel(con
   }
   __syncthreads();
 
+  // Heads in groups of 4 iterations x 4 heads: the group's loads are all
+  // issued before any arithmetic; the first group of q goes out before the
+  // token's positions are read, so the two latencies overlap.
+  constexpr int MAXIT = 4;
   for (int64_t tok = warp0; tok < tokens; tok += nwarps) {
     const int64_t b = tok / p.N;
     const int64_t n = tok - b * p.N;
+    typename Raw4<T>::type ra[MAXIT], rb[MAXIT];
+    auto load_group = [&](const HeadView& iv, int hb) {
+      const T* src0 = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + n * iv.sn + ea;
+#pragma unroll
+      for (int it = 0; it < MAXIT; ++it) {
+        const int h = hb + it * 4 + hg;
+        if (h < p.H) {
+          const T* src = src0 + int64_t(h) * iv.sh;
+          ra[it] = load_raw4<T>(src);
+          rb[it] = load_raw4<T>(src + 16);
+        } else {
+          ra[it] = rb[it] = {};
+        }
+      }
+    };
+    load_group(p.in[0], 0);
     // cos c and sin s of this lane's four frequencies.
     float c[4], sn[4];
     if (p.use_table) {
@@ -308,26 +328,11 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope2d_kernel(con
       if (t >= p.ntensor) break;
       const HeadView& iv = p.in[t];
       const HeadView& ov = p.out[t];
-      const T* src0 = static_cast<const T*>(iv.data) + iv.base + b * iv.sb + n * iv.sn + ea;
       T* dst0 = static_cast<T*>(ov.data) + ov.base + b * ov.sb + n * ov.sn + ea;
       Rope2dCoef k;
       rope2d_coef(aff[t], ea, c, sn, k);
-      // Heads in groups of 4 iterations x 4 heads: the group's loads are all
-      // issued before any arithmetic.
-      constexpr int MAXIT = 4;
       for (int hb = 0; hb < p.H; hb += 4 * MAXIT) {
-        typename Raw4<T>::type ra[MAXIT], rb[MAXIT];
-#pragma unroll
-        for (int it = 0; it < MAXIT; ++it) {
-          const int h = hb + it * 4 + hg;
-          if (h < p.H) {
-            const T* src = src0 + int64_t(h) * iv.sh;
-            ra[it] = load_raw4<T>(src);
-            rb[it] = load_raw4<T>(src + 16);
-          } else {
-            ra[it] = rb[it] = {};
-          }
-        }
+        if (t > 0 || hb > 0) load_group(iv, hb);
 #pragma unroll
         for (int it = 0; it < MAXIT; ++it) {
           if (hb + it * 4 >= p.H) break;  // warp-uniform
@@ -530,11 +535,34 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope3d_kernel(con
                          : 0.f;
   }
 
+  // Heads in groups of MAXIT warp iterations: the group's loads are all
+  // issued (kept packed) before any arithmetic; the first group's loads go
+  // out before the token's coordinates are read, so the two latencies
+  // overlap.
+  constexpr int MAXIT = 4;
   for (int64_t tok = warp0; tok < tokens; tok += nwarps) {
     const int64_t b = tok / p.L;
     const int64_t l = tok - b * p.L;
     const T* xt = static_cast<const T*>(p.x) + p.xbase + b * p.xsb + l * p.xsl + m * EPL;
     T* yt = static_cast<T*>(p.y) + p.ybase + b * p.ysb + l * p.ysl + m * EPL;
+    Pack8<T> pk[EPL == 8 ? MAXIT : 1];
+    float sv[EPL == 8 ? 1 : MAXIT][2];
+    auto load_group = [&](int hb) {
+#pragma unroll
+      for (int it = 0; it < MAXIT; ++it) {
+        const int h = hb + it * HPI + hg;
+        const T* src = xt + int64_t(h) * p.xsh;
+        const bool on = h < p.H && lane_on;
+        if constexpr (EPL == 8) {
+          if (on) pk[it] = ld_pack8<T>(src);
+          else pk[it] = Pack8<T>{};
+        } else {
+          sv[it][0] = on ? to_f(src[0]) : 0.f;
+          sv[it][1] = on ? to_f(src[1]) : 0.f;
+        }
+      }
+    };
+    load_group(0);
     float cs[NP], sn[NP];
     if (p.use_table) {
 #pragma unroll
@@ -557,25 +585,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) rope3d_kernel(con
         }
       }
     }
-    // Heads in groups of MAXIT warp iterations: the group's loads are all
-    // issued (kept packed) before any arithmetic.
-    constexpr int MAXIT = 4;
     for (int hb = 0; hb < p.H; hb += HPI * MAXIT) {
-      Pack8<T> pk[EPL == 8 ? MAXIT : 1];
-      float sv[EPL == 8 ? 1 : MAXIT][2];
-#pragma unroll
-      for (int it = 0; it < MAXIT; ++it) {
-        const int h = hb + it * HPI + hg;
-        const T* src = xt + int64_t(h) * p.xsh;
-        const bool on = h < p.H && lane_on;
-        if constexpr (EPL == 8) {
-          if (on) pk[it] = ld_pack8<T>(src);
-          else pk[it] = Pack8<T>{};
-        } else {
-          sv[it][0] = on ? to_f(src[0]) : 0.f;
-          sv[it][1] = on ? to_f(src[1]) : 0.f;
-        }
-      }
+      if (hb > 0) load_group(hb);
 #pragma unroll
       for (int it = 0; it < MAXIT; ++it) {
         if (hb + it * HPI >= p.H) break;  // warp-uniform

@@ -408,12 +408,12 @@ __global__ void __launch_bounds__(kBlock, (RES || kNV > 4) ? 2 : 3)
 // Rows of 2-8 KB without a residual branch, long inputs: one CTA per SM streams
 // its contiguous block of rows through a ring of shared-memory slots filled by
 // bulk copies (cp.async.bulk, one per row, issued by eight producer lanes of
-// warp 0, so up to `nslot` rows are in flight per SM without holding them in
-// registers); consumer warps each take every NW-th row: copy it from its
-// slot into registers, release the slot, reduce with shuffles and store the
-// normalised, modulated row directly.  The arithmetic and its order are
-// those of the register kernel above (G = 32, folded coefficients), so both
-// give identical bits.  Every mbarrier wait is bounded; on expiry the block
+// warp 0, so the rows in flight per SM are not held in registers); consumer
+// warps each take R rows at a time: copy them from their slots into
+// registers, release the slots, reduce with shuffles and store the
+// normalised, modulated rows directly.  The arithmetic and its order are
+// those of the register kernel above when it also gives a row one warp
+// (G = 32, e.g. 2048 bf16 elements), so both give identical bits there.  Every mbarrier wait is bounded; on expiry the block
 // records status 5 in g_norm_status, waits (bounded) for the copies it
 // issued and returns.
 constexpr int kRingProducers = 8;
@@ -428,7 +428,7 @@ struct RingCfg {
   uint64_t wait_ns;
 };
 
-template <typename T, int NV, int NW>
+template <typename T, int NV, int NW, int R>
 __global__ void __launch_bounds__(32 * (NW + 1), 1)
     rowring_kernel(const RowNormParams p, const RingCfg rc) {
   constexpr int VEC = 16 / int(sizeof(T));
@@ -497,93 +497,151 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
       }
     }
   } else {
-    for (int64_t k = warp - 1; k < n; k += NW) {
-      const int s = int(k % rc.nslot);
-      const uint32_t u = uint32_t(k / rc.nslot);
-      if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_norm_status)) break;
-      const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(s) * rc.row_bytes);
-      uint4 v[NV];
+    // Consumer warp w takes R consecutive rows at a time, k = R (w - 1) +
+    // R NW m: they share the coefficient loads of the output pass, and their
+    // reductions interleave.
+    for (int64_t k = int64_t(R) * (warp - 1); k < n; k += int64_t(R) * NW) {
+      const int nr = n - k < R ? int(n - k) : R;  // rows of this step (the last may be short)
+      uint4 v[R][NV];
+      bool ok = true;
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int64_t vi = lane + 32 * i;
-        v[i] = vi < nvec ? src[vi] : make_uint4(0, 0, 0, 0);
+      for (int q = 0; q < R; ++q) {
+        if (q >= nr) {
+#pragma unroll
+          for (int i = 0; i < NV; ++i) v[q][i] = make_uint4(0, 0, 0, 0);
+          continue;
+        }
+        const int s = int((k + q) % rc.nslot);
+        const uint32_t u = uint32_t((k + q) / rc.nslot);
+        if (!ring_wait(&full[s], u & 1u, abort_flag, rc.wait_ns, false, &g_norm_status)) {
+          ok = false;
+          break;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(s) * rc.row_bytes);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int64_t vi = lane + 32 * i;
+          v[q][i] = vi < nvec ? src[vi] : make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        if (lane == 0) ring_arrive(&empty[s]);
       }
-      __syncwarp();
-      if (lane == 0) ring_arrive(&empty[s]);
-      float mean = 0.f, inv = 1.f;
+      if (!ok) break;
+      float mean[R], inv[R];
       if (p.norm == NORM_LAYER) {
         // Shifted one-pass moments (shift = the row's first element), as in
         // rownorm_kernel.
-        float2 a0[P];
-        unpack2(v[0], a0, T());
-        const float K = __shfl_sync(0xffffffffu, a0[0].x, 0);
-        const float2 nk = f2(-K);
-        float2 s1 = f2(0.f), s2 = f2(0.f);
+        float K[R];
+        float2 s1[R], s2[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          float2 a0[P];
+          unpack2(v[q][0], a0, T());
+          K[q] = __shfl_sync(0xffffffffu, a0[0].x, 0);
+          s1[q] = f2(0.f);
+          s2[q] = f2(0.f);
+        }
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           if (lane + 32 * i < nvec) {
-            float2 a[P];
-            unpack2(v[i], a, T());
 #pragma unroll
-            for (int q = 0; q < P; ++q) {
-              const float2 d = add2(a[q], nk);
-              s1 = add2(s1, d);
-              s2 = fma2(d, d, s2);
+            for (int q = 0; q < R; ++q) {
+              float2 a[P];
+              unpack2(v[q][i], a, T());
+              const float2 nk = f2(-K[q]);
+#pragma unroll
+              for (int e = 0; e < P; ++e) {
+                const float2 d = add2(a[e], nk);
+                s1[q] = add2(s1[q], d);
+                s2[q] = fma2(d, d, s2[q]);
+              }
             }
           }
         }
-        float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+        float t1[R], t2[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          t1[q] = s1[q].x + s1[q].y;
+          t2[q] = s2[q].x + s2[q].y;
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-          t1 += __shfl_xor_sync(0xffffffffu, t1, o);
-          t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+#pragma unroll
+          for (int q = 0; q < R; ++q) {
+            t1[q] += __shfl_xor_sync(0xffffffffu, t1[q], o);
+            t2[q] += __shfl_xor_sync(0xffffffffu, t2[q], o);
+          }
         }
-        const float m1 = t1 / float(C);
-        mean = K + m1;
-        inv = 1.f / sqrtf(fmaxf(t2 / float(C) - m1 * m1, 0.f) + p.eps);
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          const float m1 = t1[q] / float(C);
+          mean[q] = K[q] + m1;
+          inv[q] = 1.f / sqrtf(fmaxf(t2[q] / float(C) - m1 * m1, 0.f) + p.eps);
+        }
       } else {
-        float2 acc = f2(0.f);
+        float t[R];
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          float2 a[P];
-          unpack2(v[i], a, T());
+        for (int q = 0; q < R; ++q) {
+          float2 acc = f2(0.f);
 #pragma unroll
-          for (int q = 0; q < P; ++q) acc = fma2(a[q], a[q], acc);
+          for (int i = 0; i < NV; ++i) {
+            float2 a[P];
+            unpack2(v[q][i], a, T());
+#pragma unroll
+            for (int e = 0; e < P; ++e) acc = fma2(a[e], a[e], acc);
+          }
+          t[q] = acc.x + acc.y;
         }
-        float t = acc.x + acc.y;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        inv = 1.f / sqrtf(t / float(C) + p.eps);
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+          for (int q = 0; q < R; ++q) t[q] += __shfl_xor_sync(0xffffffffu, t[q], o);
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          mean[q] = 0.f;
+          inv[q] = 1.f / sqrtf(t[q] / float(C) + p.eps);
+        }
       }
-      const int64_t row = r0 + k;
-      const int64_t bb = p.nbatch > 1 ? row / p.rows_per_batch : 0;
-      T* yr = static_cast<T*>(p.y) + row_offset(p.ym, row);
-      const float2 nm = f2(-mean), inv2 = f2(inv);
+      T* yr[R];
+      int64_t bb[R];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        const int64_t row = r0 + k + (q < nr ? q : 0);
+        bb[q] = p.nbatch > 1 ? row / p.rows_per_batch : 0;
+        yr[q] = static_cast<T*>(p.y) + row_offset(p.ym, row);
+      }
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         const int64_t vi = lane + 32 * i;
         if (vi >= nvec) continue;
         const int64_t c0 = vi * VEC;
-        float2 a[P], o[P], fa[P], fb[P];
-        unpack2(v[i], a, T());
+        float2 fa[P], fb[P], fg[P];
 #pragma unroll
-        for (int q = 0; q < P; ++q) o[q] = mul2(add2(a[q], nm), inv2);
-        const float* ca = coef + bb * C + c0;
-        const float* cb = ca + nc;
-        ld_pairs<P>(ca, fa);
-        ld_pairs<P>(cb, fb);
+        for (int q = 0; q < R; ++q) {
+          if (q >= nr) break;
+          // The coefficients are loaded once for rows of the same batch.
+          if (q == 0 || bb[q] != bb[q - 1]) {
+            const float* ca = coef + bb[q] * C + c0;
+            ld_pairs<P>(ca, fa);
+            ld_pairs<P>(ca + nc, fb);
+            if (p.g2.ptr) ld_pairs<P>(ca + 2 * nc, fg);
+          }
+          float2 a[P], o[P];
+          unpack2(v[q][i], a, T());
+          const float2 nm = f2(-mean[q]), inv2 = f2(inv[q]);
 #pragma unroll
-        for (int q = 0; q < P; ++q) o[q] = fma2(o[q], fa[q], fb[q]);
-        if (p.g2.ptr) {
-          ld_pairs<P>(cb + nc, fa);
+          for (int e = 0; e < P; ++e) o[e] = fma2(mul2(add2(a[e], nm), inv2), fa[e], fb[e]);
+          if (p.g2.ptr) {
 #pragma unroll
-          for (int q = 0; q < P; ++q) o[q] = mul2(fa[q], o[q]);
+            for (int e = 0; e < P; ++e) o[e] = mul2(fg[e], o[e]);
+          }
+          if (p.add_input) {
+#pragma unroll
+            for (int e = 0; e < P; ++e) o[e] = add2(o[e], a[e]);
+          }
+          st_act_raw(reinterpret_cast<uint4*>(yr[q] + c0), pack2(o, T()));
         }
-        if (p.add_input) {
-#pragma unroll
-          for (int q = 0; q < P; ++q) o[q] = add2(o[q], a[q]);
-        }
-        st_act_raw(reinterpret_cast<uint4*>(yr + c0), pack2(o, T()));
       }
     }
   }
@@ -687,9 +745,9 @@ static bool pick_geometry(int64_t nvec, bool scalar, int* G, int* NV) {
 constexpr int64_t kRingMinRows = 32768;
 constexpr uint32_t kRingMinRowBytes = 2048;
 
-template <typename T, int NV, int NW>
+template <typename T, int NV, int NW, int R>
 static int launch_ring(const RowNormParams& p, const RingCfg& rc, size_t smem, cudaStream_t s) {
-  auto k = rowring_kernel<T, NV, NW>;
+  auto k = rowring_kernel<T, NV, NW, R>;
   // The limit is set once per device to the most any launch of it uses.
   if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRingSmem)) != cudaSuccess) return -1;
   int64_t grid = (p.rows + NW - 1) / NW;
@@ -712,15 +770,22 @@ static int try_ring(const RowNormParams& p, cudaStream_t s) {
   rc.row_bytes = row_bytes;
   rc.coef_bytes = (size_t(p.nbatch) * size_t(p.C) * 4 * (p.g2.ptr ? 3 : 2) + 127) & ~size_t(127);
   if (rc.coef_bytes > 64 * 1024) return 0;
-  // Slot s belongs to consumer warp s % NW and to producer lane s % 8 (rows
-  // k go to slot k % nslot and warp k % NW), so nslot is a multiple of both.
-  // Each slot's owner then consumes its rows in order, so no wait on a slot
-  // barrier is ever more than one phase ahead of it: the parity of the phase
-  // waited for is never ambiguous.
-  const int nw = nv <= 8 ? 24 : 16;
-  const int64_t unit = nw == 24 ? 24 : 16;  // lcm(NW, kRingProducers)
+  // Rows up to 4 KB: 12 consumer warps taking row pairs; 8 KB rows: 16
+  // warps taking single rows (a pair would not fit the registers).  Slot s
+  // belongs to consumer warp (s / R) % NW and to producer lane s % 8 (row k
+  // goes to slot k % nslot), so nslot is a multiple of R NW and of 8: each
+  // slot's owner consumes its rows in order and no wait on a slot barrier is
+  // ever more than one phase ahead of it, so the parity of the phase waited
+  // for is never ambiguous.  Measured at 1M x 2048 bf16: one pair of slots
+  // per warp (24 slots) is fastest; shorter rows get more.
+  const bool pair = nv <= 8;
+  const int64_t unit = pair ? 24 : 16;  // lcm(R NW, kRingProducers)
   const size_t bar_bytes = size_t(2) * kRingMaxSlots * 8 + 16;
   int64_t ns = int64_t((kRingSmem - rc.coef_bytes - bar_bytes) / row_bytes);
+  if (pair) {
+    const int64_t want = unit * (4096 / row_bytes);
+    if (ns > want) ns = want;
+  }
   if (ns > kRingMaxSlots) ns = kRingMaxSlots;
   ns -= ns % unit;
   if (ns < unit) return 0;
@@ -728,10 +793,9 @@ static int try_ring(const RowNormParams& p, cudaStream_t s) {
   rc.wait_ns = 2000000000ull;
   const size_t smem = rc.coef_bytes + size_t(rc.nslot) * row_bytes + size_t(2) * rc.nslot * 8 + 16;
   int rcode;
-  if (nv <= 2) rcode = launch_ring<T, 2, 24>(p, rc, smem, s);
-  else if (nv <= 4) rcode = launch_ring<T, 4, 24>(p, rc, smem, s);
-  else if (nv <= 8) rcode = launch_ring<T, 8, 24>(p, rc, smem, s);
-  else rcode = launch_ring<T, 16, 16>(p, rc, smem, s);
+  if (nv <= 4) rcode = launch_ring<T, 4, 12, 2>(p, rc, smem, s);
+  else if (nv <= 8) rcode = launch_ring<T, 8, 12, 2>(p, rc, smem, s);
+  else rcode = launch_ring<T, 16, 16, 1>(p, rc, smem, s);
   static_assert(kRingMaxSlots % 24 == 0 && kRingMaxSlots % 16 == 0, "slot ownership");
   return rcode == 0 ? 1 : -1;
 }

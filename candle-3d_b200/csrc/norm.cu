@@ -428,7 +428,9 @@ struct RingCfg {
   uint64_t wait_ns;
 };
 
-template <typename T, int NV, int NW, int R>
+// SIMPLE: LayerNorm with one set of per-channel coefficients, no output gate,
+// no added input (the common case, with the branches compiled out).
+template <typename T, int NV, int NW, int R, bool SIMPLE>
 __global__ void __launch_bounds__(32 * (NW + 1), 1)
     rowring_kernel(const RowNormParams p, const RingCfg rc) {
   constexpr int VEC = 16 / int(sizeof(T));
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
       }
       if (!ok) break;
       float mean[R], inv[R];
-      if (p.norm == NORM_LAYER) {
+      if (SIMPLE || p.norm == NORM_LAYER) {
         // Shifted one-pass moments (shift = the row's first element), as in
         // rownorm_kernel.
         float K[R];
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
 #pragma unroll
       for (int q = 0; q < R; ++q) {
         const int64_t row = r0 + k + (q < nr ? q : 0);
-        bb[q] = p.nbatch > 1 ? row / p.rows_per_batch : 0;
+        bb[q] = (!SIMPLE && p.nbatch > 1) ? row / p.rows_per_batch : 0;
         yr[q] = static_cast<T*>(p.y) + row_offset(p.ym, row);
       }
 #pragma unroll
@@ -621,22 +623,22 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
         for (int q = 0; q < R; ++q) {
           if (q >= nr) break;
           // The coefficients are loaded once for rows of the same batch.
-          if (q == 0 || bb[q] != bb[q - 1]) {
+          if (q == 0 || (!SIMPLE && bb[q] != bb[q - 1])) {
             const float* ca = coef + bb[q] * C + c0;
             ld_pairs<P>(ca, fa);
             ld_pairs<P>(ca + nc, fb);
-            if (p.g2.ptr) ld_pairs<P>(ca + 2 * nc, fg);
+            if (!SIMPLE && p.g2.ptr) ld_pairs<P>(ca + 2 * nc, fg);
           }
           float2 a[P], o[P];
           unpack2(v[q][i], a, T());
           const float2 nm = f2(-mean[q]), inv2 = f2(inv[q]);
 #pragma unroll
           for (int e = 0; e < P; ++e) o[e] = fma2(mul2(add2(a[e], nm), inv2), fa[e], fb[e]);
-          if (p.g2.ptr) {
+          if (!SIMPLE && p.g2.ptr) {
 #pragma unroll
             for (int e = 0; e < P; ++e) o[e] = mul2(fg[e], o[e]);
           }
-          if (p.add_input) {
+          if (!SIMPLE && p.add_input) {
 #pragma unroll
             for (int e = 0; e < P; ++e) o[e] = add2(o[e], a[e]);
           }
@@ -747,7 +749,8 @@ constexpr uint32_t kRingMinRowBytes = 2048;
 
 template <typename T, int NV, int NW, int R>
 static int launch_ring(const RowNormParams& p, const RingCfg& rc, size_t smem, cudaStream_t s) {
-  auto k = rowring_kernel<T, NV, NW, R>;
+  const bool simple = p.norm == NORM_LAYER && !p.g2.ptr && !p.add_input && p.nbatch == 1;
+  auto k = simple ? rowring_kernel<T, NV, NW, R, true> : rowring_kernel<T, NV, NW, R, false>;
   // The limit is set once per device to the most any launch of it uses.
   if (set_smem_limit(reinterpret_cast<const void*>(k), int(kRingSmem)) != cudaSuccess) return -1;
   int64_t grid = (p.rows + NW - 1) / NW;

@@ -361,8 +361,8 @@ def chain_stage_reference(orc, host, C, stage, y_in=None):
 def chain_reference_cpu(orc, host, C):
     """The whole chain on the CPU oracle: f32 arithmetic on the bf16 inputs, each
     op's output rounded to bf16 as the bf16 tensors between Candle ops hold it."""
-    y = orc.round_bf16(chain_stage_reference(orc, host, C, 0))
-    y = orc.round_bf16(chain_stage_reference(orc, host, C, 1, y))
+    y = orc.round_bf16(chain_stage_reference(orc, host, C, 0), inplace=True)
+    y = orc.round_bf16(chain_stage_reference(orc, host, C, 1, y), inplace=True)
     return chain_stage_reference(orc, host, C, 2, y)
 
 

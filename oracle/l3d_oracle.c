@@ -48,6 +48,7 @@ static inline float rf16(float f) { return (float)(_Float16)f; }
 static inline float R(float f, int rnd) { return rnd == 1 ? rbf16(f) : rnd == 2 ? rf16(f) : f; }
 
 int orc_round_array(float* x, int64_t n, int rnd) {
+#pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < n; ++i) x[i] = R(x[i], rnd);
   return 0;
 }

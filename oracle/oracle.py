@@ -117,9 +117,12 @@ def use_all_host_threads() -> int:
 
 
 # ----------------------------------------------------------------- rounding
-def round_bf16(a: np.ndarray) -> np.ndarray:
-    """Round float32 values to bfloat16 (round-to-nearest-even), kept as f32."""
-    a = np.array(a, dtype=np.float32, copy=True)
+def round_bf16(a: np.ndarray, inplace: bool = False) -> np.ndarray:
+    """Round float32 values to bfloat16 (round-to-nearest-even), kept as f32;
+    `inplace` rounds a C-contiguous float32 array in place."""
+    if not (inplace and isinstance(a, np.ndarray) and a.dtype == np.float32
+            and a.flags.c_contiguous):
+        a = np.array(a, dtype=np.float32, copy=True)
     lib().orc_round_array(a, a.size, 1)
     return a
 

@@ -1293,6 +1293,11 @@ def main():
         fused = None
         if not args.no_fused_gather:
             peer = shard.PeerRows(T, C, torch.bfloat16, dev)
+        if fused is None and not args.no_fused_gather and not peer.ok:
+            fused = {"unavailable": peer.error or "another rank could not map a peer buffer"}
+            peer.close()
+            del peer
+        elif not args.no_fused_gather:
             dests = [peer.dest(p) for p in range(world)]
             dests = dests[rank:] + dests[:rank]  # the local copy first
 

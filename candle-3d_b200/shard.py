@@ -121,7 +121,8 @@ class PeerRows:
     other rank's address space with CUDA IPC, so a kernel on rank r can store
     its `rows` output rows straight into block r of every rank's buffer over
     NVLink (`dest(p)` is that block on rank p).  Collective: every rank of
-    `group` constructs it together.  `close()` (also collective) unmaps and
+    `group` constructs it together; `ok` is False on every rank when any rank
+    could not map a peer's buffer.  `close()` (also collective) unmaps and
     frees."""
 
     def __init__(self, rows: int, C: int, dtype, device, group=None):
@@ -143,22 +144,43 @@ class PeerRows:
             return res[1] if isinstance(res, tuple) and len(res) > 1 else None
 
         self._ok = ok
-        ok(rt.cudaSetDevice(self.device.index))
-        self.base = ok(rt.cudaMalloc(self.nbytes))
-        handle = ok(rt.cudaIpcGetMemHandle(self.base))
+        self.error = None
+        self.base = None
+        mine = None
+        try:
+            ok(rt.cudaSetDevice(self.device.index))
+            self.base = ok(rt.cudaMalloc(self.nbytes))
+            mine = bytes(ok(rt.cudaIpcGetMemHandle(self.base)).reserved)
+        except RuntimeError as e:  # recorded; every rank learns of it below
+            self.error = f"rank {self.rank} cannot export its buffer: {e}"
         handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle.reserved), group=group)
+        dist.all_gather_object(handles, mine, group=group)
         self.ptrs = []
         for p in range(self.world):
             if p == self.rank:
-                self.ptrs.append(int(self.base))
+                self.ptrs.append(None if self.base is None else int(self.base))
                 continue
-            h = rt.cudaIpcMemHandle_t()
-            h.reserved = handles[p]
-            self.ptrs.append(int(ok(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))))
-        n16 = self.nbytes // 2
-        raw = torch.as_tensor(_CudaArray(self.base, (n16,), "<i2"), device=self.device)
-        self.local = raw.view(dtype).view(self.world * rows, C)  # this rank's gathered rows
+            if handles[p] is None or self.base is None:
+                self.ptrs.append(None)
+                continue
+            try:
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = handles[p]
+                self.ptrs.append(int(ok(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))))
+            except RuntimeError as e:  # recorded; every rank learns of it below
+                self.error = f"rank {self.rank} cannot map rank {p}'s buffer: {e}"
+                self.ptrs.append(None)
+        # All ranks agree whether every mapping exists (a rank that failed
+        # alone must not leave the others waiting in a later collective).
+        good = self.error is None and all(h is not None for h in handles)
+        flag = torch.tensor([1 if good else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        self.ok = bool(flag.item())
+        self.local = None
+        if self.ok:
+            n16 = self.nbytes // 2
+            raw = torch.as_tensor(_CudaArray(self.base, (n16,), "<i2"), device=self.device)
+            self.local = raw.view(dtype).view(self.world * rows, C)  # this rank's gathered rows
 
     def dest(self, p: int):
         """(device pointer, element offset) of this rank's block in rank p's buffer."""
@@ -167,8 +189,9 @@ class PeerRows:
     def close(self):
         dist.barrier(group=self.group)
         for p, ptr in enumerate(self.ptrs):
-            if p != self.rank:
+            if p != self.rank and ptr is not None:
                 self._ok(self.rt.cudaIpcCloseMemHandle(ptr))
         dist.barrier(group=self.group)
         self.local = None
-        self._ok(self.rt.cudaFree(self.base))
+        if self.base is not None:
+            self._ok(self.rt.cudaFree(self.base))

@@ -9,8 +9,9 @@ add is fused with the norm that follows it:
 
   * VGGT aggregator (crate/runtime/vggt.rs:113-186,264-313): frame / global
     alternating blocks; LN -> qkv -> per-head LN + 2D RoPE (q and k, one launch)
-    -> SDPA -> proj -> LayerScale residual + norm2 (one kernel) -> fc1 ->
-    GELU-erf -> fc2 -> LayerScale residual + next block's norm1 (one kernel).
+    -> SDPA -> proj -> LayerScale residual + norm2 (one kernel) -> fc1 +
+    GELU-erf (one tcgen05 GEMM at >= 8192 rows) -> fc2 -> LayerScale residual +
+    next block's norm1 (one kernel).
   * TripoSG DiT (crate/runtime/triposg_dit.rs:217-276,346-506): sin-first
     timestep token, UViT long skips, RMSNorm-heads on the diffusers q/k/v
     split, bf16 flash cross attention, exact-GELU FFN.
@@ -33,6 +34,11 @@ import torch.nn.functional as F
 from . import ops
 
 _ATTENTION = "sdpa"
+# Rows from which the VGGT MLP's fc1 + GELU-erf runs as one tcgen05 GEMM with
+# the activation in its epilogue (measured 94.6 vs 99.8 us for cuBLAS + the
+# GELU kernel at 10,992 rows x 1024 -> 4096; slower below about 5,000 rows,
+# where its 128-row tiles leave most SMs idle).
+FUSED_MLP_MIN_ROWS = 8192
 
 
 def set_attention(impl: str) -> None:
@@ -159,7 +165,11 @@ class VggtAggregator:
                 o = self._attn(p, yv, global_pos if is_global else frame_pos)
             _, y2 = ops.residual_layer_norm_modulate(xv, o, gate=p["ls1"], weight=p["n2w"],
                                                      bias=p["n2b"], eps=1e-5, inplace=True)
-            h = ops.gelu_erf(F.linear(y2, p["fc1_w"], p["fc1_b"]))
+            if y2.numel() // C >= FUSED_MLP_MIN_ROWS:
+                # fc1 with GELU-erf in the tcgen05 GEMM epilogue (l3d_linear_ex)
+                h = ops.linear(y2, p["fc1_w"], p["fc1_b"], act="gelu_erf")
+            else:
+                h = ops.gelu_erf(F.linear(y2, p["fc1_w"], p["fc1_b"]))
             m = F.linear(h, p["fc2_w"], p["fc2_b"])
             if i + 1 < nb:
                 nxt = self.blocks[i + 1]

@@ -27,10 +27,15 @@ def attn(request, pkg):
     blocks.set_attention("sdpa")
 
 
-def test_vggt_stack_matches_reference(pkg, dev, attn):
+@pytest.mark.parametrize("fused_mlp", [False, True])
+def test_vggt_stack_matches_reference(pkg, dev, attn, fused_mlp, monkeypatch):
     import torch
 
     from candle3d_b200 import blocks
+
+    # fused_mlp: fc1 + GELU-erf as one tcgen05 GEMM at any size (normally from
+    # 8192 rows).
+    monkeypatch.setattr(blocks, "FUSED_MLP_MIN_ROWS", 0 if fused_mlp else 1 << 62)
 
     # LayerScale 1.0 instead of the 0.01 init: with 0.01 the per-block update
     # is far below one bf16 ulp of the residual stream and rounds away (in

@@ -16,7 +16,8 @@ the timed output against the CPU oracle.
 The same line carries the metric's other half, `block_stack`: tokens/s of ONE
 VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
 head-parallel), at N > 1 `block_stack_replicas` (one whole scene per GPU, the
-throughput form), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
+throughput form), at N = 1 `block_stacks_3_4` (the TripoSG and TRELLIS.2
+stacks, tokens/s), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
 `chain_c1024`, the chain at C = 1024 (its middle kernel is the VGGT per-head
 LN + 2D RoPE).
 
@@ -436,6 +437,63 @@ def chain_width_record(ops, dev, T, C, steps, warmup):
     rec["chain_GBps"] = round(12.0 * T * C / (tot / 1e3) / 1e9, 1)
     rec["launches"] = 3 * (steps + max(warmup, 3))
     del chain
+    return rec
+
+
+# ------------------------------------------- configs 3 and 4 (other stacks)
+def other_stacks_record(dev, steps, warmup):
+    """Configs 3 and 4 on one GPU, tokens/s of one model forward each: the
+    TripoSG DiT (CFG batch 2 x 2049 tokens, 21 blocks, width 2048, cross
+    attention to 1370 x 1024 tokens) and the TRELLIS.2 SLAT stack (~31.5k
+    voxels from Bernoulli(0.12) on 64^3, 24 blocks, width 1536, Q8_0 weights
+    through the dequant-linear).  Synthetic seeded inputs, random weights;
+    CUDA events around `steps` forwards after `warmup`."""
+    import torch
+
+    import __graft_entry__ as graft
+
+    graft.load_package()
+    from candle3d_b200 import blocks
+
+    g = torch.Generator().manual_seed(20261201)
+    bf = torch.bfloat16
+    stream = torch.cuda.current_stream(dev)
+    rec = {}
+    for kind in ("triposg", "trellis"):
+        if kind == "triposg":
+            model = blocks.TripoSgDit(device=dev)
+            lat = torch.randn(2, 2048, 64, generator=g).to(dev, bf)
+            cond = torch.randn(2, 1370, 1024, generator=g).to(dev, bf)
+            cond[0].zero_()
+            t = torch.tensor([1000.0 * float(torch.rand(1, generator=g))], device=dev)
+            step = lambda: model.forward(lat, t, cond)  # noqa: E731
+            tokens = 2 * 2049
+        else:
+            model = blocks.Trellis2Slat(device=dev)
+            occ = torch.rand(64, 64, 64, generator=g) < 0.12
+            coords = torch.nonzero(occ).to(torch.int32).to(dev)
+            feats = torch.randn(coords.shape[0], 32, generator=g).to(dev, bf)
+            cond = torch.randn(1, 1029, 1024, generator=g).to(dev, bf)
+            t = torch.tensor([1000.0 * float(torch.rand(1, generator=g))], device=dev)
+            step = lambda: model.forward(feats, coords, t, cond)  # noqa: E731
+            tokens = int(coords.shape[0])
+        for _ in range(max(warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        rec[kind] = {"tokens_per_s": round(tokens / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
+                     "tokens_per_step": tokens}
+        del model, step
+        torch.cuda.empty_cache()
+    rec["workloads"] = ("config3 TripoSG DiT (CFG 2 x 2049 tokens, 21 blocks, width 2048); "
+                        "config4 TRELLIS.2 SLAT (Bernoulli(0.12) voxels on 64^3, 24 blocks, "
+                        "width 1536, Q8_0 dequant-linear); one GPU, eager launches")
     return rec
 
 
@@ -1373,6 +1431,10 @@ def main():
 
         config1 = config1_record(ops, dev, None if args.no_cpu else orc)
     stack = None if args.no_stack else vggt_scene(args, world, rank, local)
+    others = None
+    if rank == 0 and world == 1 and not args.no_stack:
+        torch.cuda.empty_cache()
+        others = other_stacks_record(dev, min(args.steps, 10), args.warmup)
     stack_rep = None
     if not args.no_stack and world > 1:
         torch.cuda.empty_cache()
@@ -1403,6 +1465,7 @@ def main():
             "parity": parity,
             "block_stack": stack,
             "block_stack_replicas": stack_rep,
+            "block_stacks_3_4": others,
             "config1_fp32": config1,
             "chain_c1024": chain1024,
         }

@@ -163,9 +163,11 @@ def test_layer_norm_ring_path_rows(ops, orc, dev, dt, C, affine):
 @pytest.mark.parametrize("dt", ["bf16", "f32"])
 def test_layer_norm_modulate_ring_per_batch_chunks(ops, orc, dev, dt):
     """The ring kernel with per-batch adaLN vectors: shift / scale / gate as
-    chunk views of a [B, 6C] vector over 2 x 16400 rows of C = 1024."""
+    chunk views of a [B, 6C] vector over 2 x 16401 rows of C = 1024 (one
+    consumer's row pair then straddles the batch boundary, so the pair's
+    coefficients differ)."""
     r = rng(8)
-    B, N, C = 2, 16400, 1024
+    B, N, C = 2, 16401, 1024
     x, xv = to_dev(r.standard_normal((B, N, C)), dt, dev)
     mod, modv = to_dev(0.1 * r.standard_normal((B, 6 * C)), dt, dev)
     sh, sc, gt, *_ = ops.chunk_modulation(mod)

@@ -67,11 +67,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-stack", action="store_true",
-                    help="chain workload: skip the VGGT one-scene block_stack sub-record")
+                    help="chain workload: skip the block-stack sub-records (VGGT split scene, "
+                         "replicas, TripoSG and TRELLIS.2)")
     ap.add_argument("--no-graph", action="store_true",
                     help="VGGT stack: launch the step's kernels one by one, not as a CUDA graph")
     ap.add_argument("--no-config1", action="store_true",
-                    help="chain workload: skip the config-1 f32 micro-suite sub-record")
+                    help="chain workload: skip the config-1 f32 micro-suite and the "
+                         "C = 1024 chain sub-records")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
     ap.add_argument("--check-rows", type=int, default=8192,
                     help="rows of the timed output checked against the oracle (0: no check)")

@@ -16,7 +16,8 @@ the timed output against the CPU oracle.
 The same line carries the metric's other half, `block_stack`: tokens/s of ONE
 VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
 head-parallel), at N > 1 `block_stack_replicas` (one whole scene per GPU, the
-throughput form), at N = 1 `block_stacks_3_4` (the TripoSG and TRELLIS.2
+throughput form) and `trellis_split` (one TRELLIS.2 scene's voxel rows split
+over the N GPUs), at N = 1 `block_stacks_3_4` (the TripoSG and TRELLIS.2
 stacks, tokens/s), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
 `chain_c1024`, the chain at C = 1024 (its middle kernel is the VGGT per-head
 LN + 2D RoPE).
@@ -496,6 +497,77 @@ def other_stacks_record(dev, steps, warmup):
     rec["workloads"] = ("config3 TripoSG DiT (CFG 2 x 2049 tokens, 21 blocks, width 2048); "
                         "config4 TRELLIS.2 SLAT (Bernoulli(0.12) voxels on 64^3, 24 blocks, "
                         "width 1536, Q8_0 dequant-linear); one GPU, eager launches")
+    return rec
+
+
+def trellis_split_record(args, world, rank, local):
+    """Config 4 (TRELLIS.2 SLAT, ~31.5k voxels, 24 blocks, Q8_0) with ONE
+    scene's sorted voxel rows split over the `world` ranks (shard.shard_range):
+    every op runs on the rank's rows except the self-attention, which
+    exchanges q/k/v head-parallel (12 heads, so world must divide 12); the
+    final outputs are gathered.  Tokens/s of the one scene, and rank 0's rerun
+    of the whole scene alone against the gathered output."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as graft
+
+    graft.load_package()
+    from candle3d_b200 import blocks, shard
+
+    if 12 % world:
+        return {"unavailable": f"12 attention heads do not split over {world} ranks"}
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(20261201)
+    bf = torch.bfloat16
+    model = blocks.Trellis2Slat(device=dev)
+    occ = torch.rand(64, 64, 64, generator=g) < 0.12
+    coords = torch.nonzero(occ).to(torch.int32).to(dev)
+    feats = torch.randn(coords.shape[0], 32, generator=g).to(dev, bf)
+    cond = torch.randn(1, 1029, 1024, generator=g).to(dev, bf)
+    t = torch.tensor([1000.0 * float(torch.rand(1, generator=g))], device=dev)
+    ntot = int(coords.shape[0])
+    counts = [shard.shard_range(ntot, world, r)[1] - shard.shard_range(ntot, world, r)[0]
+              for r in range(world)]
+    a0, a1 = shard.shard_range(ntot, world, rank)
+    split = shard.SceneSplit()
+    f_loc, c_loc = feats[a0:a1].contiguous(), coords[a0:a1].contiguous()
+
+    def step():
+        out = model.forward(f_loc, c_loc, t, cond, split=split, counts=counts)
+        return shard.gather_rows(out, ntot, world)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    steps = min(args.steps, 10)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        out = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    tt = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    rec = {"tokens_per_s": round(ntot / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
+           "tokens_per_step": ntot,
+           "parallelism": f"one scene, voxel rows split over {world} GPUs ({counts[0]} rows on "
+                          f"rank 0), self-attention head-parallel ({12 // world} heads per rank, "
+                          "2 NCCL all-to-alls per block), final all-gather; eager launches"}
+    if rank == 0:
+        single = model.forward(feats, coords, t, cond).float()
+        d = out.float() - single
+        rel = float(d.norm() / single.norm())
+        rec["parity_vs_single_gpu"] = {"rel_l2": rel, "max_abs": float(d.abs().max()),
+                                       "tol": "rel L2 < 2e-2 (bf16 stack)", "ok": rel < 2e-2}
+    torch.cuda.synchronize()
+    dist.barrier()
+    del model
+    torch.cuda.empty_cache()
     return rec
 
 
@@ -1437,10 +1509,12 @@ def main():
     if rank == 0 and world == 1 and not args.no_stack:
         torch.cuda.empty_cache()
         others = other_stacks_record(dev, min(args.steps, 10), args.warmup)
-    stack_rep = None
+    stack_rep = trellis_split = None
     if not args.no_stack and world > 1:
         torch.cuda.empty_cache()
         stack_rep = vggt_scene(args, world, rank, local, replicas=True)
+        torch.cuda.empty_cache()
+        trellis_split = trellis_split_record(args, world, rank, local)
 
     if rank == 0:
         line = {
@@ -1468,6 +1542,7 @@ def main():
             "block_stack": stack,
             "block_stack_replicas": stack_rep,
             "block_stacks_3_4": others,
+            "trellis_split": trellis_split,
             "config1_fp32": config1,
             "chain_c1024": chain1024,
         }

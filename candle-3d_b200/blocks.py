@@ -456,21 +456,62 @@ class Trellis2Slat:
         return [ops.chunk_modulation((p["modulation"].unsqueeze(0) + temb).contiguous())
                 for p in self.blocks]
 
-    def forward(self, feats, coords, t_model, cond):
-        """feats [N, in_ch], coords [N, 3] int32, cond [1, Lc, cond_dim] -> [N, in_ch]."""
+    def _self_attn_split(self, p, y, coords, split, counts):
+        """Self-attention over all voxels when the voxel rows are split across
+        the ranks of `split` (shard.SceneSplit; rank r owns counts[r]
+        consecutive rows of the sorted voxel list, y [1, L, C], coords [L, 3]):
+        q / k are normed and rotated on the local rows per head group straight
+        into the head-group-major send buffer, exchanged head-parallel (uneven
+        slabs), attended over all voxels and sent back to their owners."""
+        _, L, C = y.shape
+        H, D, world = self.H, self.D, split.world
+        h = H // world
+        qkv = p["to_qkv"](y).view(1, L, 3, H, D)
+        send = torch.empty(world, L, 3, h, D, dtype=y.dtype, device=y.device)
+        for j in range(world):
+            hs = slice(j * h, (j + 1) * h)
+            ops.qk_l2norm_rope3d(qkv[:, :, 0, hs], p["qg"][hs], coords, out=send[j:j + 1, :, 0])
+            ops.qk_l2norm_rope3d(qkv[:, :, 1, hs], p["kg"][hs], coords, out=send[j:j + 1, :, 1])
+        send[:, :, 2].copy_(qkv[0, :, 2].view(L, world, h, D).transpose(0, 1))
+        q, k, v = split.exchange_qkv_uneven(send, counts)
+        total = int(sum(counts))
+        if _ATTENTION == "l3d":
+            a = torch.empty(total, h, D, dtype=y.dtype, device=y.device)
+            ops.attention(q, k, v, out=a.permute(1, 0, 2).unsqueeze(0))
+        else:
+            a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).contiguous()
+        o = split.return_heads_uneven(a, counts)
+        return p["to_out"](o.view(1, L, C))
+
+    def forward(self, feats, coords, t_model, cond, split=None, counts=None):
+        """feats [N, in_ch], coords [N, 3] int32, cond [1, Lc, cond_dim] -> [N, in_ch].
+
+        With `split` (shard.SceneSplit over W ranks whose heads divide 12) and
+        `counts` (rows per rank), feats / coords are this rank's consecutive
+        rows of the sorted voxel list and the result is those rows' output:
+        every op is per voxel except the self-attention, which exchanges q/k/v
+        head-parallel across the ranks."""
         N = feats.shape[0]
         C, H, D = self.C, self.H, self.D
+        if split is not None and split.world > 1:
+            if H % split.world or counts is None or int(counts[split.rank]) != N:
+                raise ValueError("a split needs heads divisible by the ranks and this rank's count")
+        else:
+            split = None
         x = F.linear(feats, *self.input_layer).view(1, N, C).contiguous()
         mods = self.block_mods(self.t_emb(t_model))
         y = ops.layer_norm_modulate(x, mods[0][0], mods[0][1], eps=1e-6)
         Lc = cond.shape[1]
         for i, p in enumerate(self.blocks):
             sh_msa, sc_msa, g_msa, sh_mlp, sc_mlp, g_mlp = mods[i]
-            qkv = p["to_qkv"](y).view(1, N, 3, H, D)
-            q = ops.qk_l2norm_rope3d(qkv[:, :, 0], p["qg"], coords)
-            k = ops.qk_l2norm_rope3d(qkv[:, :, 1], p["kg"], coords)
-            a = _attend(q.transpose(1, 2), k.transpose(1, 2), qkv[:, :, 2].transpose(1, 2))
-            o = p["to_out"](a.transpose(1, 2).reshape(1, N, C))
+            if split is not None:
+                o = self._self_attn_split(p, y, coords, split, counts)
+            else:
+                qkv = p["to_qkv"](y).view(1, N, 3, H, D)
+                q = ops.qk_l2norm_rope3d(qkv[:, :, 0], p["qg"], coords)
+                k = ops.qk_l2norm_rope3d(qkv[:, :, 1], p["kg"], coords)
+                a = _attend(q.transpose(1, 2), k.transpose(1, 2), qkv[:, :, 2].transpose(1, 2))
+                o = p["to_out"](a.transpose(1, 2).reshape(1, N, C))
             x, y = ops.residual_layer_norm_modulate(x, o, gate=g_msa, weight=p["n2w"], bias=p["n2b"],
                                                     eps=1e-6, inplace=True)
             cq = ops.qk_l2norm_rope3d(p["c_q"](y).view(1, N, H, D), p["cqg"], None)

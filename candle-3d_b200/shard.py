@@ -98,6 +98,34 @@ class SceneSplit:
         r = self.all_to_all(out_tokens).view(self.world, L, h, D)
         return r.permute(1, 0, 2, 3).reshape(L, self.world * h * D)
 
+    # ---- slabs of unequal length (rank j owns counts[j] tokens)
+    def exchange_qkv_uneven(self, send: torch.Tensor, counts):
+        """As exchange_qkv when the ranks' slabs differ in length: send
+        [world, L, 3, h, D] with L = counts[rank]; returns q, k, v as
+        [1, h, sum(counts), D] views (token order = rank order)."""
+        world, L, three, h, D = send.shape
+        total = int(sum(counts))
+        if self.world == 1:
+            r = send.view(L, 3, h, D)
+        else:
+            r = send.new_empty((total, 3, h, D))
+            dist.all_to_all_single(r, send.contiguous().view(world * L, 3, h, D),
+                                   output_split_sizes=list(counts), input_split_sizes=[L] * world,
+                                   group=self.group)
+        return tuple(r[:, i].permute(1, 0, 2).unsqueeze(0) for i in range(3))
+
+    def return_heads_uneven(self, out_tokens: torch.Tensor, counts) -> torch.Tensor:
+        """As return_heads for unequal slabs: out_tokens [sum(counts), h, D]
+        -> [counts[rank], world * h * D] rows of this rank's tokens."""
+        total, h, D = out_tokens.shape
+        L = int(counts[self.rank])
+        if self.world == 1:
+            return out_tokens.reshape(L, h * D)
+        r = out_tokens.new_empty((self.world * L, h, D))
+        dist.all_to_all_single(r, out_tokens.contiguous(), output_split_sizes=[L] * self.world,
+                               input_split_sizes=list(counts), group=self.group)
+        return r.view(self.world, L, h, D).permute(1, 0, 2, 3).reshape(L, self.world * h * D)
+
     def all_gather_rows(self, local: torch.Tensor) -> torch.Tensor:
         """[L, ...] slabs of every rank -> [world * L, ...] in rank order."""
         if self.world == 1:

@@ -16,8 +16,9 @@ the timed output against the CPU oracle.
 The same line carries the metric's other half, `block_stack`: tokens/s of ONE
 VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
 head-parallel), at N > 1 `block_stack_replicas` (one whole scene per GPU, the
-throughput form) and `trellis_split` (one TRELLIS.2 scene's voxel rows split
-over the N GPUs), at N = 1 `block_stacks_3_4` (the TripoSG and TRELLIS.2
+throughput form), `trellis_split` (one TRELLIS.2 scene's voxel rows split
+over the N GPUs) and `triposg_split` (the TripoSG CFG batch split by element,
+and beyond two GPUs each element's tokens too), at N = 1 `block_stacks_3_4` (the TripoSG and TRELLIS.2
 stacks, tokens/s), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
 `chain_c1024`, the chain at C = 1024 (its middle kernel is the VGGT per-head
 LN + 2D RoPE).
@@ -71,7 +72,8 @@ def parse():
                     help="chain workload: skip the block-stack sub-records (VGGT split scene, "
                          "replicas, TripoSG and TRELLIS.2)")
     ap.add_argument("--no-graph", action="store_true",
-                    help="VGGT stack: launch the step's kernels one by one, not as a CUDA graph")
+                    help="block stacks: launch each step's kernels one by one, not as one "
+                         "CUDA-graph replay")
     ap.add_argument("--no-config1", action="store_true",
                     help="chain workload: skip the config-1 f32 micro-suite and the "
                          "C = 1024 chain sub-records")
@@ -444,7 +446,40 @@ def chain_width_record(ops, dev, T, C, steps, warmup):
 
 
 # ------------------------------------------- configs 3 and 4 (other stacks)
-def other_stacks_record(dev, steps, warmup):
+def graphed(step, enabled=True):
+    """`step` (already warmed up on every rank) captured once as a CUDA graph:
+    returns (run, graph), run() replays it and returns the captured output.
+    At a fraction of a scene per GPU the host-side launch of each op takes
+    longer than the op, which the replay removes.  Without `enabled`, (step,
+    None).  A graph that holds NCCL calls must be released before the process
+    group is destroyed."""
+    import torch
+
+    if not enabled:
+        return step, None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = step()
+    graph.replay()
+    torch.cuda.synchronize()
+    return (lambda: (graph.replay(), out)[1]), graph
+
+
+def time_steps(run, steps, stream):
+    """Mean CUDA-event time (ms) of `steps` calls of run() on `stream`."""
+    import torch
+
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def other_stacks_record(dev, steps, warmup, graph=True):
     """Configs 3 and 4 on one GPU, tokens/s of one model forward each: the
     TripoSG DiT (CFG batch 2 x 2049 tokens, 21 blocks, width 2048, cross
     attention to 1370 x 1024 tokens) and the TRELLIS.2 SLAT stack (~31.5k
@@ -482,21 +517,17 @@ def other_stacks_record(dev, steps, warmup):
             tokens = int(coords.shape[0])
         for _ in range(max(warmup, 3)):
             step()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
+        eager = time_steps(step, steps, stream)
+        run, gr = graphed(step, graph)
+        ms = time_steps(run, steps, stream)
         rec[kind] = {"tokens_per_s": round(tokens / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
-                     "tokens_per_step": tokens}
-        del model, step
+                     "tokens_per_step": tokens, "ms_per_step_eager": round(eager, 3)}
+        del model, step, run, gr
         torch.cuda.empty_cache()
     rec["workloads"] = ("config3 TripoSG DiT (CFG 2 x 2049 tokens, 21 blocks, width 2048); "
                         "config4 TRELLIS.2 SLAT (Bernoulli(0.12) voxels on 64^3, 24 blocks, "
-                        "width 1536, Q8_0 dequant-linear); one GPU, eager launches")
+                        "width 1536, Q8_0 dequant-linear); one GPU, "
+                        + ("one CUDA-graph replay per forward" if graph else "eager launches"))
     return rec
 
 
@@ -542,22 +573,20 @@ def trellis_split_record(args, world, rank, local):
         step()
     torch.cuda.synchronize()
     dist.barrier()
-    steps = min(args.steps, 10)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        out = step()
-    e1.record(stream)
-    torch.cuda.synchronize()
+    run, graph = graphed(step, not args.no_graph)
     dist.barrier()
-    tt = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    out = run()
+    steps = min(args.steps, 10)
+    tt = torch.tensor([time_steps(run, steps, stream)], dtype=torch.float64, device=dev)
+    dist.barrier()
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = float(tt.item())
+    launches = "one CUDA-graph replay per step" if graph is not None else "eager launches"
     rec = {"tokens_per_s": round(ntot / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
            "tokens_per_step": ntot,
            "parallelism": f"one scene, voxel rows split over {world} GPUs ({counts[0]} rows on "
                           f"rank 0), self-attention head-parallel ({12 // world} heads per rank, "
-                          "2 NCCL all-to-alls per block), final all-gather; eager launches"}
+                          f"2 NCCL all-to-alls per block), final all-gather; {launches}"}
     if rank == 0:
         single = model.forward(feats, coords, t, cond).float()
         d = out.float() - single
@@ -566,7 +595,79 @@ def trellis_split_record(args, world, rank, local):
                                        "tol": "rel L2 < 2e-2 (bf16 stack)", "ok": rel < 2e-2}
     torch.cuda.synchronize()
     dist.barrier()
-    del model
+    del model, run, graph  # the graph holds NCCL calls: released before the group goes
+    torch.cuda.empty_cache()
+    return rec
+
+
+def triposg_split_record(args, world, rank, local):
+    """Config 3 (TripoSG DiT, CFG batch 2 x (1 + 2048) tokens, 21 blocks,
+    width 2048) with the batch split over the ranks (shard.BatchTokenSplit):
+    the [uncond, cond] elements go to two halves of the ranks, and with more
+    than two ranks each element's token sequence is split over its half
+    (self-attention head-parallel inside the half, 16 heads; the cross
+    attention reads all encoder tokens on every rank).  Tokens/s of the one
+    CFG batch, and rank 0's rerun of the whole batch alone against the
+    gathered output."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as graft
+
+    graft.load_package()
+    from candle3d_b200 import blocks, shard
+
+    if world % 2 or 16 % (world // 2):
+        return {"unavailable": f"a CFG batch of 2 with 16 heads does not split over {world} ranks"}
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(20261201)
+    bf = torch.bfloat16
+    model = blocks.TripoSgDit(device=dev)
+    lat = torch.randn(2, 2048, 64, generator=g).to(dev, bf)
+    cond = torch.randn(2, 1370, 1024, generator=g).to(dev, bf)
+    cond[0].zero_()
+    t = torch.tensor([1000.0 * float(torch.rand(1, generator=g))], device=dev)
+    bts = shard.BatchTokenSplit(2, 2048, world)
+    groups = [dist.new_group(r) for r in bts.groups()] if bts.per > 1 else None
+    b, lo, hi, prefix = bts.rows(rank)
+    split = shard.SceneSplit(groups[b]) if groups else None
+    lat_loc, cond_loc = lat[b:b + 1, lo:hi].contiguous(), cond[b:b + 1].contiguous()
+
+    def step():
+        out = model.forward(lat_loc, t, cond_loc, split=split, counts=bts.counts, prefix=prefix)
+        return bts.gather(out[0])
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    run, graph = graphed(step, not args.no_graph)
+    dist.barrier()
+    out = run()
+    steps = min(args.steps, 10)
+    tt = torch.tensor([time_steps(run, steps, stream)], dtype=torch.float64, device=dev)
+    dist.barrier()
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    launches = "one CUDA-graph replay per step" if graph is not None else "eager launches"
+    ntok = 2 * 2049
+    rec = {"tokens_per_s": round(ntok / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
+           "tokens_per_step": ntok,
+           "parallelism": (f"CFG batch split: [uncond, cond] on {bts.per} GPU(s) each"
+                           + (f", tokens split {bts.counts} with head-parallel self-attention "
+                              f"({16 // bts.per} heads per rank, 2 NCCL all-to-alls per block)"
+                              if bts.per > 1 else ", no communication")
+                           + f"; final all-gather; {launches}")}
+    if rank == 0:
+        single = model.forward(lat, t, cond).float()
+        d = out.float() - single
+        rel = float(d.norm() / single.norm())
+        rec["parity_vs_single_gpu"] = {"rel_l2": rel, "max_abs": float(d.abs().max()),
+                                       "tol": "rel L2 < 2e-2 (bf16 stack)", "ok": rel < 2e-2}
+    torch.cuda.synchronize()
+    dist.barrier()
+    del model, run, graph  # the graph holds NCCL calls: released before the group goes
     torch.cuda.empty_cache()
     return rec
 
@@ -1508,13 +1609,15 @@ def main():
     others = None
     if rank == 0 and world == 1 and not args.no_stack:
         torch.cuda.empty_cache()
-        others = other_stacks_record(dev, min(args.steps, 10), args.warmup)
-    stack_rep = trellis_split = None
+        others = other_stacks_record(dev, min(args.steps, 10), args.warmup, not args.no_graph)
+    stack_rep = trellis_split = triposg_split = None
     if not args.no_stack and world > 1:
         torch.cuda.empty_cache()
         stack_rep = vggt_scene(args, world, rank, local, replicas=True)
         torch.cuda.empty_cache()
         trellis_split = trellis_split_record(args, world, rank, local)
+        torch.cuda.empty_cache()
+        triposg_split = triposg_split_record(args, world, rank, local)
 
     if rank == 0:
         line = {
@@ -1543,6 +1646,7 @@ def main():
             "block_stack_replicas": stack_rep,
             "block_stacks_3_4": others,
             "trellis_split": trellis_split,
+            "triposg_split": triposg_split,
             "config1_fp32": config1,
             "chain_c1024": chain1024,
         }

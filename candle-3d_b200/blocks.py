@@ -271,6 +271,30 @@ class TripoSgDit:
         a = _attend(q, k, v)
         return F.linear(a.transpose(1, 2).reshape(B, L, C), p["o1_w"], p["o1_b"])
 
+    def _self_attn_split(self, p, y, split, counts):
+        """Self-attention over one batch element's whole token sequence when
+        its tokens are split across the ranks of `split` (shard.SceneSplit;
+        rank r owns counts[r] consecutive tokens, y [1, L, C]): the RMS-normed
+        q / k and v are written head-group-major into the send buffer,
+        exchanged head-parallel, attended over all tokens and sent back."""
+        _, L, C = y.shape
+        H, D, world = self.H, self.D, split.world
+        h = H // world
+        qkv = F.linear(y, p["qkv1_w"]).view(L, world, h, 3 * D)
+        send = torch.empty(world, L, 3, h, D, dtype=y.dtype, device=y.device)
+        ops.rms_norm_heads(qkv[..., :D], p["nq1"], 1e-6, out=send[:, :, 0].transpose(0, 1))
+        ops.rms_norm_heads(qkv[..., D:2 * D], p["nk1"], 1e-6, out=send[:, :, 1].transpose(0, 1))
+        send[:, :, 2].copy_(qkv[..., 2 * D:].transpose(0, 1))
+        q, k, v = split.exchange_qkv_uneven(send, counts)
+        total = int(sum(counts))
+        if _ATTENTION == "l3d":
+            a = torch.empty(total, h, D, dtype=y.dtype, device=y.device)
+            ops.attention(q, k, v, out=a.permute(1, 0, 2).unsqueeze(0))
+        else:
+            a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).contiguous()
+        o = split.return_heads_uneven(a, counts)
+        return F.linear(o.view(1, L, C), p["o1_w"], p["o1_b"])
+
     def _cross_attn(self, p, y, cond):
         B, L, C = y.shape
         H, D = self.H, self.D
@@ -289,10 +313,30 @@ class TripoSgDit:
         h = ops.linear_small(h, self.t2[0], self.t2[1])
         return h.view(1, 1, self.C).expand(B, 1, self.C)
 
-    def forward(self, latents, t, cond):
+    def forward(self, latents, t, cond, split=None, counts=None, prefix=True):
+        """latents [B, L, 64], cond [B, S, 1024] -> [B, L, 64].
+
+        With `split` (shard.SceneSplit over W ranks, 16 heads divisible by W)
+        and `counts` (tokens per rank of the 1 + L token sequence, the
+        timestep token first), latents [1, l, 64] are this rank's latent rows
+        of one batch element, cond that element's encoder tokens, `prefix`
+        whether this rank's slab starts with the timestep token, and the
+        result is those rows' output [1, l, 64]: every op is per token except
+        the self-attention, which exchanges q/k/v head-parallel (the cross
+        attention reads all of cond on every rank)."""
         B, L, _ = latents.shape
         C = self.C
-        x = torch.cat([self.timestep_token(t, B), F.linear(latents, *self.proj_in)], 1).contiguous()
+        if split is not None and split.world > 1:
+            if (B != 1 or self.H % split.world or counts is None
+                    or int(counts[split.rank]) != L + int(prefix)):
+                raise ValueError("a split needs one batch element, heads divisible by the ranks "
+                                 "and this rank's token count")
+        else:
+            split, prefix = None, True
+        x = F.linear(latents, *self.proj_in)
+        if prefix:
+            x = torch.cat([self.timestep_token(t, B), x], 1)
+        x = x.contiguous()
         mid = self.layers // 2
         skips = []
         y = None  # norm1 output of the current block when fused upstream
@@ -304,8 +348,8 @@ class TripoSgDit:
                 y = None
             if y is None:
                 y = ops.layer_norm(x, p["n1w"], p["n1b"], 1e-5)
-            x, y = ops.residual_layer_norm_modulate(x, self._self_attn(p, y), weight=p["n2w"],
-                                                    bias=p["n2b"], eps=1e-5)
+            a = self._self_attn(p, y) if split is None else self._self_attn_split(p, y, split, counts)
+            x, y = ops.residual_layer_norm_modulate(x, a, weight=p["n2w"], bias=p["n2b"], eps=1e-5)
             x, y = ops.residual_layer_norm_modulate(x, self._cross_attn(p, y, cond),
                                                     weight=p["n3w"], bias=p["n3b"], eps=1e-5)
             ff = F.linear(ops.gelu_erf(F.linear(y, p["ff1_w"], p["ff1_b"])), p["ff2_w"], p["ff2_b"])

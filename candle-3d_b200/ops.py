@@ -88,11 +88,12 @@ def residual_layer_norm_modulate(x, h, gate=None, weight=None, bias=None, shift=
     return r, y
 
 
-def rms_norm_heads(x, weight, eps=1e-6):
+def rms_norm_heads(x, weight, eps=1e-6, out=None):
     """RmsNormHeads::rms_norm_heads (crate/runtime/triposg_dit.rs:511-522).
-    Output is contiguous in x's logical shape (strided chunk views accepted)."""
+    Output is contiguous in x's logical shape (strided chunk views accepted),
+    or written into `out` (x's shape, rows strided, last dim contiguous)."""
     _check_cuda(x, weight)
-    y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    y = torch.empty(x.shape, dtype=x.dtype, device=x.device) if out is None else out
     call("l3d_rms_norm_heads", ref(desc(x)), ref(desc(weight)), eps, ref(desc(y)), _s(x))
     return y
 

@@ -135,6 +135,55 @@ class SceneSplit:
         return out
 
 
+# ------------------------------------------- batch elements x token slabs
+class BatchTokenSplit:
+    """A batch of `batch` sequences, each `1 + L` tokens long (one prefix token,
+    then L rows whose outputs are kept), spread over `world` ranks: batch
+    element b goes to the `world / batch` consecutive ranks of group b, which
+    split its token sequence into slabs (shard_range).  This is the TripoSG
+    CFG split (crate/runtime/triposg_dit.rs:619-621: the [uncond, cond]
+    batch of 2, each element an independent DiT forward) and, with more than
+    one rank per element, the token split of each element.
+
+    `rows(rank)` gives a rank's batch element and its slab of the L kept rows
+    [lo, hi) (the slab of rank 0 of a group starts with the prefix token,
+    which is not one of them); `counts` the slab lengths of the group's ranks
+    (prefix included) for SceneSplit's uneven exchange."""
+
+    def __init__(self, batch: int, L: int, world: int):
+        if batch <= 0 or world <= 0 or world % batch:
+            raise ValueError(f"{world} ranks do not split a batch of {batch}")
+        self.batch, self.L, self.world = batch, L, world
+        self.per = world // batch
+        self.counts = [shard_range(1 + L, self.per, r)[1] - shard_range(1 + L, self.per, r)[0]
+                       for r in range(self.per)]
+
+    def rows(self, rank: int) -> tuple[int, int, int, bool]:
+        """(batch element, lo, hi, holds the prefix token) of `rank`."""
+        b, g = divmod(rank, self.per)
+        a0, a1 = shard_range(1 + self.L, self.per, g)
+        return b, max(a0 - 1, 0), a1 - 1, a0 == 0
+
+    def groups(self):
+        """The ranks of each batch element's group, in batch order."""
+        return [list(range(b * self.per, (b + 1) * self.per)) for b in range(self.batch)]
+
+    def gather(self, local: torch.Tensor, group=None) -> torch.Tensor:
+        """local [hi - lo, F] rows of this rank -> [batch, L, F] on every rank
+        (one all-gather of row blocks padded to the longest slab)."""
+        F = local.shape[-1]
+        if self.world == 1:
+            return local.reshape(1, self.L, F)
+        spans = [self.rows(r)[1:3] for r in range(self.world)]
+        cap = max(hi - lo for lo, hi in spans)
+        padded = local.new_zeros((cap, F))
+        padded[: local.shape[0]] = local
+        out = local.new_empty((self.world * cap, F))
+        dist.all_gather_into_tensor(out, padded, group=group)
+        parts = [out[r * cap: r * cap + hi - lo] for r, (lo, hi) in enumerate(spans)]
+        return torch.cat(parts, 0).view(self.batch, self.L, F)
+
+
 # ------------------------------------------ gather buffers in peer memory
 class _CudaArray:
     """Raw device memory described through __cuda_array_interface__."""

@@ -226,3 +226,75 @@ def test_scene_split_uneven_slabs_match_unsplit_attention():
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=10) for _ in range(2))
     assert res == {0: True, 1: True}
+
+
+def test_batch_token_split_layout():
+    """The CFG batch x token slabs of BatchTokenSplit tile each element's L
+    kept rows exactly once, only a group's first rank holds the prefix token,
+    and the counts (prefix included) sum to 1 + L."""
+    import __graft_entry__ as g
+
+    g.load_package()
+    from candle3d_b200 import shard
+
+    for world in (1, 2, 4, 8):
+        for L in (2048, 7):
+            bts = shard.BatchTokenSplit(2, L, world) if world > 1 else None
+            if bts is None:
+                with pytest.raises(ValueError):
+                    shard.BatchTokenSplit(2, L, world)
+                continue
+            assert sum(bts.counts) == 1 + L
+            seen = {0: [], 1: []}
+            for r in range(world):
+                b, lo, hi, prefix = bts.rows(r)
+                assert prefix == (r % bts.per == 0)
+                assert hi - lo + int(prefix) == bts.counts[r % bts.per]
+                seen[b].extend(range(lo, hi))
+            assert seen[0] == list(range(L)) and seen[1] == list(range(L))
+
+
+def _batch_token_worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as g
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g.load_package()
+        from candle3d_b200 import shard
+
+        L, F = 37, 5
+        full = torch.arange(2 * L * F, dtype=torch.float32).view(2, L, F)
+        bts = shard.BatchTokenSplit(2, L, world)
+        b, lo, hi, _ = bts.rows(rank)
+        got = bts.gather(full[b, lo:hi].contiguous())
+        q.put((rank, bool(torch.equal(got, full))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_batch_token_split_gathers_every_row(world):
+    """gloo world size 2 and 4: each rank's slab of one batch element,
+    gathered, rebuilds the [2, L, F] output exactly."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batch_token_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    res = dict(q.get(timeout=10) for _ in range(world))
+    assert res == {r: True for r in range(world)}

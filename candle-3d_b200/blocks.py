@@ -500,46 +500,51 @@ class Trellis2Slat:
         return [ops.chunk_modulation((p["modulation"].unsqueeze(0) + temb).contiguous())
                 for p in self.blocks]
 
-    def _self_attn_split(self, p, y, coords, split, counts):
+    def _self_attn_split(self, p, y, coords, split, counts, groups):
         """Self-attention over all voxels when the voxel rows are split across
         the ranks of `split` (shard.SceneSplit; rank r owns counts[r]
         consecutive rows of the sorted voxel list, y [1, L, C], coords [L, 3]):
         q / k are normed and rotated on the local rows per head group straight
         into the head-group-major send buffer, exchanged head-parallel (uneven
-        slabs), attended over all voxels and sent back to their owners."""
+        slabs; with `groups` < world head groups each group is shared by
+        world / groups ranks, which split its queries), attended over all
+        voxels and sent back to their owners."""
         _, L, C = y.shape
-        H, D, world = self.H, self.D, split.world
-        h = H // world
+        H, D = self.H, self.D
+        h = H // groups
         qkv = p["to_qkv"](y).view(1, L, 3, H, D)
-        send = torch.empty(world, L, 3, h, D, dtype=y.dtype, device=y.device)
-        for j in range(world):
+        send = torch.empty(groups, L, 3, h, D, dtype=y.dtype, device=y.device)
+        for j in range(groups):
             hs = slice(j * h, (j + 1) * h)
             ops.qk_l2norm_rope3d(qkv[:, :, 0, hs], p["qg"][hs], coords, out=send[j:j + 1, :, 0])
             ops.qk_l2norm_rope3d(qkv[:, :, 1, hs], p["kg"][hs], coords, out=send[j:j + 1, :, 1])
-        send[:, :, 2].copy_(qkv[0, :, 2].view(L, world, h, D).transpose(0, 1))
-        q, k, v = split.exchange_qkv_uneven(send, counts)
-        total = int(sum(counts))
+        send[:, :, 2].copy_(qkv[0, :, 2].view(L, groups, h, D).transpose(0, 1))
+        q, k, v = split.exchange_qkv_uneven(send, counts, groups)
         if _ATTENTION == "l3d":
-            a = torch.empty(total, h, D, dtype=y.dtype, device=y.device)
+            a = torch.empty(q.shape[2], h, D, dtype=y.dtype, device=y.device)
             ops.attention(q, k, v, out=a.permute(1, 0, 2).unsqueeze(0))
         else:
             a = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).contiguous()
-        o = split.return_heads_uneven(a, counts)
+        o = split.return_heads_uneven(a, counts, groups)
         return p["to_out"](o.view(1, L, C))
 
-    def forward(self, feats, coords, t_model, cond, split=None, counts=None):
+    def forward(self, feats, coords, t_model, cond, split=None, counts=None, head_groups=None):
         """feats [N, in_ch], coords [N, 3] int32, cond [1, Lc, cond_dim] -> [N, in_ch].
 
-        With `split` (shard.SceneSplit over W ranks whose heads divide 12) and
-        `counts` (rows per rank), feats / coords are this rank's consecutive
-        rows of the sorted voxel list and the result is those rows' output:
-        every op is per voxel except the self-attention, which exchanges q/k/v
-        head-parallel across the ranks."""
+        With `split` (shard.SceneSplit over W ranks) and `counts` (rows per
+        rank), feats / coords are this rank's consecutive rows of the sorted
+        voxel list and the result is those rows' output: every op is per voxel
+        except the self-attention, which exchanges q/k/v head-parallel across
+        the ranks in `head_groups` groups (default gcd(12, W); each group is
+        shared by W / head_groups ranks, which split its queries)."""
         N = feats.shape[0]
         C, H, D = self.C, self.H, self.D
         if split is not None and split.world > 1:
-            if H % split.world or counts is None or int(counts[split.rank]) != N:
-                raise ValueError("a split needs heads divisible by the ranks and this rank's count")
+            G = math.gcd(H, split.world) if head_groups is None else int(head_groups)
+            if (H % G or split.world % G or counts is None
+                    or int(counts[split.rank]) != N):
+                raise ValueError("a split needs head groups dividing the heads and the ranks, "
+                                 "and this rank's count")
         else:
             split = None
         x = F.linear(feats, *self.input_layer).view(1, N, C).contiguous()
@@ -549,7 +554,7 @@ class Trellis2Slat:
         for i, p in enumerate(self.blocks):
             sh_msa, sc_msa, g_msa, sh_mlp, sc_mlp, g_mlp = mods[i]
             if split is not None:
-                o = self._self_attn_split(p, y, coords, split, counts)
+                o = self._self_attn_split(p, y, coords, split, counts, G)
             else:
                 qkv = p["to_qkv"](y).view(1, N, 3, H, D)
                 q = ops.qk_l2norm_rope3d(qkv[:, :, 0], p["qg"], coords)

@@ -99,32 +99,66 @@ class SceneSplit:
         return r.permute(1, 0, 2, 3).reshape(L, self.world * h * D)
 
     # ---- slabs of unequal length (rank j owns counts[j] tokens)
-    def exchange_qkv_uneven(self, send: torch.Tensor, counts):
+    #
+    # With `groups` = G < world head groups (H not divisible by the ranks; G
+    # divides world), the ranks form world / G query blocks of G consecutive
+    # ranks: rank r attends head group r % G for the queries of its block's
+    # tokens (the slabs of ranks [b G, (b + 1) G), b = r // G) over all keys.
+    # Each token's q / k / v of head group j then go to the world / G ranks
+    # that attend group j, and each rank gets its tokens' outputs back from
+    # the G ranks of its own block.  G = world is the plain head-parallel case.
+    def _groups(self, groups):
+        G = self.world if groups is None else int(groups)
+        if G <= 0 or self.world % G:
+            raise ValueError(f"{G} head groups do not tile {self.world} ranks")
+        return G
+
+    def query_block(self, counts, groups=None) -> tuple[int, int]:
+        """Token range [start, end) of this rank's query block."""
+        G = self._groups(groups)
+        b = self.rank // G
+        return int(sum(counts[:b * G])), int(sum(counts[:(b + 1) * G]))
+
+    def exchange_qkv_uneven(self, send: torch.Tensor, counts, groups=None):
         """As exchange_qkv when the ranks' slabs differ in length: send
-        [world, L, 3, h, D] with L = counts[rank]; returns q, k, v as
-        [1, h, sum(counts), D] views (token order = rank order)."""
-        world, L, three, h, D = send.shape
+        [G, L, 3, h, D] with L = counts[rank] (head group j at [j]); returns
+        q over this rank's query block [1, h, block tokens, D] and k, v over
+        all tokens [1, h, sum(counts), D] (token order = rank order)."""
+        G = self._groups(groups)
+        g, L, three, h, D = send.shape
         total = int(sum(counts))
         if self.world == 1:
             r = send.view(L, 3, h, D)
         else:
+            if G < self.world:  # head group r % G for every destination rank r
+                idx = torch.arange(self.world, device=send.device) % G
+                send = send.index_select(0, idx)
             r = send.new_empty((total, 3, h, D))
-            dist.all_to_all_single(r, send.contiguous().view(world * L, 3, h, D),
-                                   output_split_sizes=list(counts), input_split_sizes=[L] * world,
-                                   group=self.group)
-        return tuple(r[:, i].permute(1, 0, 2).unsqueeze(0) for i in range(3))
+            dist.all_to_all_single(r, send.contiguous().view(self.world * L, 3, h, D),
+                                   output_split_sizes=list(counts),
+                                   input_split_sizes=[L] * self.world, group=self.group)
+        q0, q1 = self.query_block(counts, G)
+        q = r[q0:q1, 0].permute(1, 0, 2).unsqueeze(0)
+        return (q,) + tuple(r[:, i].permute(1, 0, 2).unsqueeze(0) for i in (1, 2))
 
-    def return_heads_uneven(self, out_tokens: torch.Tensor, counts) -> torch.Tensor:
-        """As return_heads for unequal slabs: out_tokens [sum(counts), h, D]
-        -> [counts[rank], world * h * D] rows of this rank's tokens."""
-        total, h, D = out_tokens.shape
+    def return_heads_uneven(self, out_tokens: torch.Tensor, counts, groups=None) -> torch.Tensor:
+        """As return_heads for unequal slabs: out_tokens [block tokens, h, D]
+        (this rank's head group over its query block) -> [counts[rank],
+        G * h * D] rows of this rank's tokens, channel = head * D + d."""
+        G = self._groups(groups)
+        _, h, D = out_tokens.shape
         L = int(counts[self.rank])
         if self.world == 1:
             return out_tokens.reshape(L, h * D)
-        r = out_tokens.new_empty((self.world * L, h, D))
-        dist.all_to_all_single(r, out_tokens.contiguous(), output_split_sizes=[L] * self.world,
-                               input_split_sizes=list(counts), group=self.group)
-        return r.view(self.world, L, h, D).permute(1, 0, 2, 3).reshape(L, self.world * h * D)
+        b = self.rank // G
+        mine = [i // G == b for i in range(self.world)]
+        r = out_tokens.new_empty((G * L, h, D))
+        dist.all_to_all_single(r, out_tokens.contiguous(),
+                               output_split_sizes=[L if m else 0 for m in mine],
+                               input_split_sizes=[int(counts[i]) if m else 0
+                                                  for i, m in enumerate(mine)],
+                               group=self.group)
+        return r.view(G, L, h, D).permute(1, 0, 2, 3).reshape(L, G * h * D)
 
     def all_gather_rows(self, local: torch.Tensor) -> torch.Tensor:
         """[L, ...] slabs of every rank -> [world * L, ...] in rank order."""

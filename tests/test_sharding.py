@@ -298,3 +298,65 @@ def test_batch_token_split_gathers_every_row(world):
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=10) for _ in range(world))
     assert res == {r: True for r in range(world)}
+
+
+def _shared_groups_worker(rank, world, port, q, H, groups):
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    import __graft_entry__ as g
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g.load_package()
+        from candle3d_b200 import shard
+
+        Ntot, D = 83, 8
+        counts = [shard.shard_range(Ntot, world, r)[1] - shard.shard_range(Ntot, world, r)[0]
+                  for r in range(world)]
+        a0, a1 = shard.shard_range(Ntot, world, rank)
+        gen = torch.Generator().manual_seed(13)
+        qkv = torch.randn(Ntot, 3, H, D, generator=gen)
+        full = F.scaled_dot_product_attention(*(qkv[:, i].transpose(0, 1)[None] for i in range(3)))
+        full = full[0].transpose(0, 1).reshape(Ntot, H * D)
+        split = shard.SceneSplit()
+        h = H // groups
+        L = a1 - a0
+        send = qkv[a0:a1].view(L, 3, groups, h, D).permute(2, 0, 1, 3, 4).contiguous()
+        qh, kh, vh = split.exchange_qkv_uneven(send, counts, groups)
+        b0, b1 = split.query_block(counts, groups)
+        ok = qh.shape == (1, h, b1 - b0, D) and kh.shape == (1, h, Ntot, D)
+        a = F.scaled_dot_product_attention(qh, kh, vh)[0].transpose(0, 1).contiguous()
+        o = split.return_heads_uneven(a, counts, groups)
+        ok = ok and torch.allclose(o, full[a0:a1], atol=1e-6, rtol=1e-5)
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,H,groups", [(4, 6, 2), (4, 12, 4), (4, 6, 1), (2, 3, 1)])
+def test_scene_split_shared_head_groups_match_unsplit_attention(world, H, groups):
+    """Fewer head groups than ranks (the TRELLIS.2 split at 8 ranks: 12 heads
+    in 4 groups, each shared by 2 ranks that split its queries): gloo world
+    sizes 2 and 4, 83 rows in uneven slabs, against the unsplit attention."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shared_groups_worker, args=(r, world, port, q, H, groups))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    res = dict(q.get(timeout=10) for _ in range(world))
+    assert res == {r: True for r in range(world)}

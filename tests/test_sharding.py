@@ -281,9 +281,9 @@ def _batch_token_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_batch_token_split_gathers_every_row(world):
-    """gloo world size 2 and 4: each rank's slab of one batch element,
+    """gloo world sizes 2, 4 and 8: each rank's slab of one batch element,
     gathered, rebuilds the [2, L, F] output exactly."""
     import torch.multiprocessing as mp
 
@@ -341,11 +341,12 @@ def _shared_groups_worker(rank, world, port, q, H, groups):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,H,groups", [(4, 6, 2), (4, 12, 4), (4, 6, 1), (2, 3, 1)])
+@pytest.mark.parametrize("world,H,groups", [(4, 6, 2), (4, 12, 4), (4, 6, 1), (2, 3, 1),
+                                            (8, 12, 4)])
 def test_scene_split_shared_head_groups_match_unsplit_attention(world, H, groups):
     """Fewer head groups than ranks (the TRELLIS.2 split at 8 ranks: 12 heads
     in 4 groups, each shared by 2 ranks that split its queries): gloo world
-    sizes 2 and 4, 83 rows in uneven slabs, against the unsplit attention."""
+    sizes 2, 4 and 8, 83 rows in uneven slabs, against the unsplit attention."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")

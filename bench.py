@@ -18,10 +18,11 @@ VGGT config-2 scene split over the N GPUs (frame blocks by view, global blocks
 head-parallel), at N > 1 `block_stack_replicas` (one whole scene per GPU, the
 throughput form), `trellis_split` (one TRELLIS.2 scene's voxel rows split
 over the N GPUs) and `triposg_split` (the TripoSG CFG batch split by element,
-and beyond two GPUs each element's tokens too), at N = 1 `block_stacks_3_4` (the TripoSG and TRELLIS.2
-stacks, tokens/s), and at N = 1 `config1_fp32`, the f32 micro-suite per op, and
-`chain_c1024`, the chain at C = 1024 (its middle kernel is the VGGT per-head
-LN + 2D RoPE).
+and beyond two GPUs each element's tokens too); at N = 1 `block_stacks_3_4`
+(the TripoSG and TRELLIS.2 stacks, tokens/s), `config1_fp32`, the f32
+micro-suite per op, `chain_c1024`, the chain at C = 1024 (its middle kernel is
+the VGGT per-head LN + 2D RoPE), and `sweep_c5`, config 5's rows x channels
+sweep.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Multi-GPU: launched by torch.distributed.run, one rank per GPU; every rank
@@ -75,8 +76,8 @@ def parse():
                     help="block stacks: launch each step's kernels one by one, not as one "
                          "CUDA-graph replay")
     ap.add_argument("--no-config1", action="store_true",
-                    help="chain workload: skip the config-1 f32 micro-suite and the "
-                         "C = 1024 chain sub-records")
+                    help="chain workload: skip the config-1 f32 micro-suite, the "
+                         "C = 1024 chain and the config-5 rows x channels sweep sub-records")
     ap.add_argument("--cpu-sample-rows", type=int, default=8192)
     ap.add_argument("--check-rows", type=int, default=8192,
                     help="rows of the timed output checked against the oracle (0: no check)")
@@ -442,6 +443,69 @@ def chain_width_record(ops, dev, T, C, steps, warmup):
     rec["chain_GBps"] = round(12.0 * T * C / (tot / 1e3) / 1e9, 1)
     rec["launches"] = 3 * (steps + max(warmup, 3))
     del chain
+    return rec
+
+
+def sweep_record(ops, dev, rows=(4096, 32768, 262144, 1 << 20), widths=(1024, 1536, 2048),
+                 launches=20):
+    """BASELINE config 5's sweep on one GPU: the chain (LN + modulate -> QK norm
+    + RoPE -> GELU-tanh, bf16) at every rows x channels point.  Inputs have
+    config 5's distributions, drawn on the device (parity of the same kernels
+    is checked elsewhere; only the timing is taken here).  Each point times
+    `launches` chain steps captured as one CUDA graph, rotating through enough
+    input / output sets that the sets exceed 4x the 126 MB L2, so that every
+    point reads HBM; the 4k-row points are still bound by launch ramp-up and
+    tail (a step there moves 25-50 MB).  GB/s = 12 B per element per step."""
+    import math
+
+    import torch
+
+    peak, peak_kind = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(20261201)
+    stream = torch.cuda.current_stream(dev)
+    rec = {"peak": peak, "peak_source": peak_kind, "launches_per_point": 3 * launches,
+           "points": []}
+    for C in widths:
+        H, D, kind = head_cfg(C)
+        shift = (0.1 * torch.randn(C, device=dev, generator=g)).to(torch.bfloat16)
+        scale = (0.1 * torch.randn(C, device=dev, generator=g)).to(torch.bfloat16)
+        if kind == "rope2d":
+            params = ((1 + 0.02 * torch.randn(D, device=dev, generator=g)).to(torch.bfloat16),
+                      (0.02 * torch.randn(D, device=dev, generator=g)).to(torch.bfloat16))
+        else:
+            params = ((1 + 0.02 * torch.randn(H, D, device=dev, generator=g)).float(),)
+        for T in rows:
+            i = torch.arange(T, device=dev)
+            if kind == "rope2d":
+                aux = torch.stack([i // 64 % 64 + 1, i % 64 + 1], -1).reshape(1, T, 2)
+            else:
+                aux = torch.stack([(i // 4096) % 64, (i // 64) % 64, i % 64], -1)
+            aux = aux.to(torch.int32)
+            nsets = max(1, math.ceil(4 * 126e6 / (3 * 2 * T * C)))
+            chains = [Chain(ops, {"x": torch.randn(T, C, device=dev, generator=g).to(torch.bfloat16),
+                                  "shift": shift, "scale": scale, "aux": aux, "params": params},
+                            T, C) for _ in range(nsets)]
+            for c in chains[:3]:
+                c.step()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for k in range(launches):
+                    chains[k % nsets].step()
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / launches
+            gbs = 12.0 * T * C / (ms / 1e3) / 1e9
+            rec["points"].append({"rows": T, "channels": C, "ms_per_step": round(ms, 4),
+                                  "GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
+                                  "input_sets": nsets})
+            del chains, graph
+            torch.cuda.empty_cache()
     return rec
 
 
@@ -1601,9 +1665,12 @@ def main():
     # the N GPUs; and, at N = 1, config 1 (the f32 micro-suite)
     del chain, inp
     torch.cuda.empty_cache()
-    config1 = chain1024 = None
+    config1 = chain1024 = sweep = None
     if rank == 0 and world == 1 and not args.no_config1 and C != 1024:
         chain1024 = chain_width_record(ops, dev, T, 1024, args.steps, args.warmup)
+        torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_config1:
+        sweep = sweep_record(ops, dev)
         torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_config1:
         from oracle import oracle as orc
@@ -1653,6 +1720,7 @@ def main():
             "triposg_split": triposg_split,
             "config1_fp32": config1,
             "chain_c1024": chain1024,
+            "sweep_c5": sweep,
         }
         print(json.dumps(line))
     if world > 1:

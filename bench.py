@@ -410,6 +410,38 @@ def time_cpu_chain(orc, C, rows, seed, min_seconds=10.0):
     return 12.0 * rows * C * n / el / 1e9, n, el
 
 
+def host_cpu_model():
+    """The host CPU's model name (lscpu's "Model name"), or None."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline_record(orc, C, rows, seconds=10.0, one_core_seconds=5.0):
+    """The C oracle's chain on the host: on every core this process may use
+    (the reported baseline), and on one core beside it, with the host's CPU
+    model.  Each is a bounded sample: passes over `rows` rows until the time
+    is spent."""
+    cores = orc.use_all_host_threads()
+    gbs, n, el = time_cpu_chain(orc, C, rows, 7, min_seconds=seconds)
+    rec = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+           "sample": f"{n} passes of {rows} rows x C={C} ({el:.1f} s), C oracle",
+           "host_cpu": host_cpu_model()}
+    orc.lib().orc_set_num_threads(1)
+    try:
+        g1, n1, e1 = time_cpu_chain(orc, C, rows, 7, min_seconds=one_core_seconds)
+    finally:
+        orc.use_all_host_threads()
+    rec["one_core"] = {"value": round(g1, 3), "unit": "GB/s", "cores": 1,
+                       "sample": f"{n1} passes of {rows} rows x C={C} ({e1:.1f} s)"}
+    return rec
+
+
 # ------------------------------------------------ a second chain width
 def chain_width_record(ops, dev, T, C, steps, warmup):
     """The config-5 chain at another width on one GPU (C = 1024 swaps in the
@@ -1656,10 +1688,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle as orc
 
-        orc.use_all_host_threads()
-        gbs, n, el = time_cpu_chain(orc, C, args.cpu_sample_rows, 7, min_seconds=10.0)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": orc.num_threads(), "kind": "port",
-               "sample": f"{n} passes of {args.cpu_sample_rows} rows x C={C} ({el:.1f} s), C oracle"}
+        cpu = cpu_baseline_record(orc, C, args.cpu_sample_rows)
 
     # ---- the other half of the metric: tokens/s of one VGGT scene split over
     # the N GPUs; and, at N = 1, config 1 (the f32 micro-suite)

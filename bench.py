@@ -581,7 +581,9 @@ def other_stacks_record(dev, steps, warmup, graph=True):
     attention to 1370 x 1024 tokens) and the TRELLIS.2 SLAT stack (~31.5k
     voxels from Bernoulli(0.12) on 64^3, 24 blocks, width 1536, Q8_0 weights
     through the dequant-linear).  Synthetic seeded inputs, random weights;
-    CUDA events around `steps` forwards after `warmup`."""
+    CUDA events around `steps` forwards after `warmup`, launched one by one
+    (`ms_per_step_eager`) and, with `graph`, as one CUDA-graph replay each
+    (the reported tokens/s)."""
     import torch
 
     import __graft_entry__ as graft

@@ -179,7 +179,9 @@ struct Layout {
 // ----------------------------------------------------------------- device
 // One stream per device, as candle_core::CudaDevice.  Storage comes from the
 // allocator (stream-ordered cudaMallocAsync by default); a host that owns a
-// pool passes its own.
+// pool passes its own.  As with Candle's CudaDevice, the device must be the
+// calling thread's current one (cudaSetDevice) while its ops are issued: the
+// kernels go to `stream`, which belongs to it.
 struct Storage {
   void* ptr = nullptr;
   size_t bytes = 0;
@@ -201,7 +203,9 @@ struct Device {
     if (bytes == 0) return st;
     int cur = -1;
     cudaError_t e = cudaGetDevice(&cur);
-    if (e == cudaSuccess && cur != ordinal) e = cudaSetDevice(ordinal);
+    if (e == cudaSuccess && cur != ordinal)
+      throw Error(L3D_E_CUDA, "alloc on cuda:" + std::to_string(ordinal) + ": the thread's current "
+                              "device is cuda:" + std::to_string(cur) + " (cudaSetDevice first)");
     if (e == cudaSuccess) e = cudaMallocAsync(&st->ptr, bytes, stream);
     if (e != cudaSuccess) {
       cudaGetLastError();
@@ -299,6 +303,19 @@ class Tensor {
   Tensor gelu() const { return unary(l3d_gelu_tanh, "gelu"); }
   Tensor gelu_erf() const { return unary(l3d_gelu_erf, "gelu_erf"); }
   Tensor silu() const { return unary(l3d_silu, "silu"); }
+  // GeGlu::forward (crate/runtime/nn_blocks.rs:250-253): x [.., 2F] ->
+  // x[.., :F] * gelu_erf(x[.., F:]).
+  Tensor geglu() const {
+    if (!is_float(dtype_)) throw Error(L3D_E_DTYPE, std::string("geglu: unsupported dtype ") + as_str(dtype_));
+    if (rank() == 0 || layout_.dims.back() % 2)
+      throw Error(L3D_E_SHAPE, "geglu: last dim of " + dims_str(layout_.dims) + " is not even");
+    std::vector<int64_t> od = layout_.dims;
+    od.back() /= 2;
+    Tensor y = empty(od, dtype_, dev_);
+    const l3d_tensor xd = desc(), yd = y.desc();
+    check(l3d_geglu(&xd, &yd, dev_.stream), "l3d_geglu");
+    return y;
+  }
 
  private:
   Tensor view(Layout l) const { return Tensor(st_, std::move(l), dtype_, dev_); }
@@ -417,7 +434,75 @@ inline Tensor rope_fused(const Tensor& x, const Tensor& cos_full, const Tensor& 
   return y;
 }
 
+// exact_sdpa_heads (crate/runtime/attention_math.rs:199-259), non-causal:
+// softmax(q k^T * scale) v per (batch, head) on the tensor cores.  q [B, H, N,
+// D], k / v [B, H, Nk, D] bf16 views with the head dim contiguous (D = 64 or
+// 128), read in place.  `status`, when given, receives the kernel's status
+// word storage (4 bytes at its start; 0 = every bounded wait completed),
+// readable after the stream is synchronised.
+inline Tensor sdpa(const Tensor& q, const Tensor& k, const Tensor& v, float scale,
+                   std::shared_ptr<Storage>* status = nullptr) {
+  const char* op = "sdpa";
+  using namespace ::l3d::candle::detail;
+  require_rank(q, 4, op, "q");
+  require_rank(k, 4, op, "k");
+  require_dims(v, k.dims(), op, "v");
+  if (q.dtype() != DType::BF16 || k.dtype() != DType::BF16 || v.dtype() != DType::BF16)
+    throw Error(L3D_E_DTYPE, "sdpa: q, k and v are bf16");
+  if (k.dim(0) != q.dim(0) || k.dim(1) != q.dim(1) || k.dim(3) != q.dim(3))
+    throw Error(L3D_E_SHAPE, "sdpa: q " + dims_str(q.dims()) + " and k " + dims_str(k.dims()) +
+                                 " differ in batch, heads or head dim");
+  if (!(scale > 0.f)) throw Error(L3D_E_SHAPE, "sdpa: scale must be positive");
+  Tensor y = q.empty_like();
+  const size_t need = l3d_attention_workspace_size(k.dim(0), k.dim(1), k.dim(2), k.dim(3));
+  std::shared_ptr<Storage> ws = q.device().alloc(need);
+  const l3d_tensor qd = q.desc(), kd = k.desc(), vd = v.desc(), yd = y.desc();
+  check(l3d_attention(&qd, &kd, &vd, scale, &yd, ws->ptr, ws->bytes, q.device().stream),
+        "l3d_attention");
+  if (status) *status = ws;
+  return y;
+}
+
 }  // namespace ops
+
+// candle_nn::Linear::forward / ops::mul_mat_add on an unquantised bf16 weight
+// [n, k] (crate/runtime/nn_blocks.rs:82,179-195), with the element-wise ops
+// the blocks apply next fused into the GEMM epilogue:
+//   y = residual + gate * act(x . W^T + bias)
+// (Mlp fc1 + gelu_erf, crate/runtime/nn_blocks.rs:219-236; the LayerScale
+// residual x + ls * proj(..), crate/runtime/vggt.rs:118-121).
+enum class Act { None = 0, Silu = 1, GeluErf = 2, GeluTanh = 3 };
+
+struct Linear {
+  Tensor weight;
+  std::optional<Tensor> bias;
+
+  Tensor forward(const Tensor& x, Act act = Act::None, const std::optional<Tensor>& residual = {},
+                 const std::optional<Tensor>& gate = {}) const {
+    const char* op = "linear";
+    using namespace ::l3d::candle::detail;
+    require_rank(weight, 2, op, "weight");
+    if (weight.dtype() != DType::BF16) throw Error(L3D_E_DTYPE, "linear: weight is bf16");
+    const int64_t n = weight.dim(0), k = weight.dim(1);
+    if (last_dim(x, op) != k)
+      throw Error(L3D_E_SHAPE, "linear: x " + dims_str(x.dims()) + " against weight " +
+                                   dims_str(weight.dims()));
+    if (bias) require_dims(*bias, {n}, op, "bias");
+    std::vector<int64_t> od = x.dims();
+    od.back() = n;
+    if (residual) require_dims(*residual, od, op, "residual");
+    if (gate && !residual) throw Error(L3D_E_SHAPE, "linear: a gate needs a residual");
+    Tensor y = Tensor::empty(od, DType::BF16, x.device());
+    const int64_t m = x.elem_count() / k;
+    std::shared_ptr<Storage> ws = x.device().alloc(l3d_linear_workspace_size(m, n, k));
+    l3d_tensor bs{}, rs{}, gs{};
+    const l3d_tensor xd = x.desc(), wd = weight.desc(), yd = y.desc();
+    check(l3d_linear_ex(&xd, &wd, opt_desc(bias, bs), int(act), opt_desc(residual, rs),
+                        opt_desc(gate, gs), &yd, ws->ptr, ws->bytes, x.device().stream),
+          "l3d_linear_ex");
+    return y;
+  }
+};
 
 // candle_nn::LayerNorm { weight, bias, eps } (affine or not).
 struct LayerNorm {
@@ -564,6 +649,97 @@ inline Tensor timestep_embedding(const Tensor& t, int64_t dim, TimestepOrder ord
   return y;
 }
 
+// The block seam: residual, then the next (modulated) norm, one pass
+// (crate/runtime/vggt.rs:118-121; crate/runtime/trellis2_blocks.rs:632-642):
+//   r = x + [gate *] h;  y = LN(r) [* w + b] [* (1 + scale) + shift].
+// Returns (r, y).
+inline std::pair<Tensor, Tensor> residual_layer_norm_modulate(
+    const Tensor& x, const Tensor& h, const std::optional<Tensor>& gate,
+    const std::optional<Tensor>& weight, const std::optional<Tensor>& bias,
+    const std::optional<Tensor>& shift, const std::optional<Tensor>& scale, float eps) {
+  const char* op = "residual-layer-norm-modulate";
+  detail::require_float(x, op, "x");
+  detail::require_dims(h, x.dims(), op, "h");
+  Tensor r = x.empty_like(), y = x.empty_like();
+  l3d_tensor gs{}, ws{}, bs{}, shs{}, scs{};
+  const l3d_tensor xd = x.desc(), hd = h.desc(), rd = r.desc(), yd = y.desc();
+  check(l3d_residual_layer_norm_modulate(
+            &xd, &hd, detail::opt_desc(gate, gs), detail::opt_desc(weight, ws),
+            detail::opt_desc(bias, bs), detail::opt_desc(shift, shs), detail::opt_desc(scale, scs),
+            eps, &rd, &yd, x.device().stream),
+        "l3d_residual_layer_norm_modulate");
+  return {r, y};
+}
+
+// The small per-step linears (Trellis2AdaLn, the timestep MLPs, modulation +
+// t_emb; crate/runtime/trellis2_blocks.rs:209-258,617,
+// crate/runtime/triposg_dit.rs:295-299): y = act_out(act_in(x) . w^T + bias +
+// addend), x [B, K] with B <= 16, w [N, K].
+inline Tensor linear_small(const Tensor& x, const Tensor& w, const std::optional<Tensor>& bias,
+                           const std::optional<Tensor>& addend, nn::Act act_in, nn::Act act_out) {
+  const char* op = "linear-small";
+  detail::require_rank(x, 2, op, "x");
+  detail::require_rank(w, 2, op, "w");
+  if (w.dim(1) != x.dim(1))
+    throw Error(L3D_E_SHAPE, "linear-small: x " + dims_str(x.dims()) + " against w " +
+                                 dims_str(w.dims()));
+  Tensor y = Tensor::empty({x.dim(0), w.dim(0)}, x.dtype(), x.device());
+  l3d_tensor bs{}, as{};
+  const l3d_tensor xd = x.desc(), wd = w.desc(), yd = y.desc();
+  check(l3d_linear_small(&xd, &wd, detail::opt_desc(bias, bs), detail::opt_desc(addend, as),
+                         int(act_in), int(act_out), &yd, x.device().stream),
+        "l3d_linear_small");
+  return y;
+}
+
+// PatchEmbed + prepare_tokens (crate/runtime/pi3_encoder.rs:116-126,219-231):
+// pixels [BS, Cin, H, W], weight [C, Cin, p, p], bias [C], pos [1 + np, C],
+// cls [C], reg [R, C] or none -> [BS, 1 + R + np, C].
+inline Tensor patch_embed(const Tensor& pixels, const Tensor& weight, const Tensor& bias,
+                          const Tensor& pos, const Tensor& cls, const std::optional<Tensor>& reg,
+                          int64_t patch) {
+  const char* op = "patch-embed";
+  detail::require_rank(pixels, 4, op, "pixels");
+  detail::require_rank(weight, 4, op, "weight");
+  if (patch <= 0 || pixels.dim(2) % patch || pixels.dim(3) % patch)
+    throw Error(L3D_E_SHAPE, "patch-embed: image " + dims_str(pixels.dims()) +
+                                 " is not whole patches of " + std::to_string(patch));
+  const int64_t np = (pixels.dim(2) / patch) * (pixels.dim(3) / patch);
+  const int64_t R = reg ? reg->dim(0) : 0;
+  Tensor y = Tensor::empty({pixels.dim(0), 1 + R + np, weight.dim(0)}, pixels.dtype(),
+                           pixels.device());
+  l3d_tensor rs{};
+  const l3d_tensor px = pixels.desc(), wd = weight.desc(), bd = bias.desc(), pd = pos.desc(),
+                   cd = cls.desc(), yd = y.desc();
+  check(l3d_patch_embed(&px, &wd, &bd, &pd, &cd, detail::opt_desc(reg, rs), int(patch), &yd,
+                        pixels.device().stream),
+        "l3d_patch_embed");
+  return y;
+}
+
+// CoordMap + the per-offset pair loops (crate/runtime/trellis2_sparse.rs:
+// 68-106,211-236): coords [N, 3] i32 -> pair_dest, pair_src [27, N] and counts
+// [27] (i32), offset k's pairs in ascending destination order.
+struct NeighborPairs {
+  Tensor pair_dest, pair_src, counts;
+};
+inline NeighborPairs neighbor_pairs(const Tensor& coords) {
+  const char* op = "neighbor-pairs";
+  detail::require_rank(coords, 2, op, "coords");
+  if (coords.dim(1) != 3 || coords.dtype() != DType::I32)
+    throw Error(L3D_E_SHAPE, "neighbor-pairs: coords are [N, 3] i32");
+  const int64_t n = coords.dim(0);
+  const Device& d = coords.device();
+  NeighborPairs p{Tensor::empty({27, n}, DType::I32, d), Tensor::empty({27, n}, DType::I32, d),
+                  Tensor::empty({27}, DType::I32, d)};
+  std::shared_ptr<Storage> ws = d.alloc(l3d_sparse_neighbor_pairs_workspace_size(n));
+  const l3d_tensor cd = coords.desc(), dd = p.pair_dest.desc(), sd = p.pair_src.desc(),
+                   nd = p.counts.desc();
+  check(l3d_sparse_neighbor_pairs(&cd, &dd, &sd, &nd, ws->ptr, ws->bytes, d.stream),
+        "l3d_sparse_neighbor_pairs");
+  return p;
+}
+
 // index_select_rows (crate/runtime/trellis2_sparse.rs:118-133).
 inline Tensor index_select_rows(const Tensor& feats, const Tensor& ids) {
   const char* op = "index-select-rows";
@@ -614,7 +790,14 @@ class QMatMul {
   int64_t k() const { return k_; }
   size_t weight_bytes() const { return size_t(n_ * (k_ / block_elems(fmt_)) * block_bytes(fmt_)); }
 
-  Tensor forward(const Tensor& x) const {
+  Tensor forward(const Tensor& x) const { return forward_ex(x, nn::Act::None, {}, {}); }
+
+  // With the block's next element-wise ops in the GEMM epilogue:
+  // y = residual + gate * act(x . deq(W)^T + bias) (Trellis2FeedForward's
+  // mlp.0 + gelu, crate/runtime/trellis2_blocks.rs:558-561; the gated
+  // residuals :632-633, :644-645).
+  Tensor forward_ex(const Tensor& x, nn::Act act, const std::optional<Tensor>& residual,
+                    const std::optional<Tensor>& gate) const {
     const char* op = "qmatmul";
     candle::detail::require_float(x, op, "x");
     if (candle::detail::last_dim(x, op) != k_)
@@ -622,15 +805,28 @@ class QMatMul {
                                    std::to_string(k_));
     std::vector<int64_t> od = x.dims();
     od.back() = n_;
-    Tensor y = Tensor::empty(od, x.dtype() == DType::F32 ? DType::F32 : DType::BF16, x.device());
+    if (residual) candle::detail::require_dims(*residual, od, op, "residual");
+    if (gate && !residual) throw Error(L3D_E_SHAPE, "qmatmul: a gate needs a residual");
+    const DType yt = residual ? residual->dtype() : (x.dtype() == DType::F32 ? DType::F32 : DType::BF16);
+    Tensor y = Tensor::empty(od, yt, x.device());
     const int64_t m = x.elem_count() / k_;
     const size_t need = l3d_dequant_linear_workspace_size(int(fmt_), m, n_, k_);
     if (!ws_ || ws_->bytes < need) ws_ = x.device().alloc(need);
-    l3d_tensor bs{};
+    l3d_tensor bs{}, rs{}, gs{};
     const l3d_tensor xd = x.desc(), yd = y.desc();
-    check(l3d_dequant_linear(&xd, blocks_, int(fmt_), n_, k_, candle::detail::opt_desc(bias_, bs),
-                             &yd, ws_->ptr, ws_->bytes, x.device().stream),
-          "l3d_dequant_linear");
+    if (act == nn::Act::None && !residual) {
+      check(l3d_dequant_linear(&xd, blocks_, int(fmt_), n_, k_,
+                               candle::detail::opt_desc(bias_, bs), &yd, ws_->ptr, ws_->bytes,
+                               x.device().stream),
+            "l3d_dequant_linear");
+    } else {
+      check(l3d_dequant_linear_ex(&xd, blocks_, int(fmt_), n_, k_,
+                                  candle::detail::opt_desc(bias_, bs), int(act),
+                                  candle::detail::opt_desc(residual, rs),
+                                  candle::detail::opt_desc(gate, gs), &yd, ws_->ptr, ws_->bytes,
+                                  x.device().stream),
+            "l3d_dequant_linear_ex");
+    }
     return y;
   }
 

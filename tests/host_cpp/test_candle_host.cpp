@@ -109,6 +109,28 @@ static void host_checks() {
   EXPECT(qm.weight_bytes() == 64 * 4 * 34);
   EXPECT_ERROR(qm.forward(fake({3, 96}, DType::BF16)), L3D_E_SHAPE, "last dim must be 128");
   EXPECT(QMatMul(kFake, GgmlDType::Q4K, 8, 256).weight_bytes() == 8 * 144);
+  EXPECT_ERROR(qm.forward_ex(fake({3, 128}, DType::BF16), nn::Act::GeluTanh, std::nullopt,
+                             fake({64}, DType::F32)),
+               L3D_E_SHAPE, "gate needs a residual");
+  EXPECT_ERROR(fake({2, 7}, DType::BF16).geglu(), L3D_E_SHAPE, "not even");
+  Tensor qa = fake({1, 4, 16, 64}, DType::BF16), ka = fake({1, 4, 32, 64}, DType::BF16);
+  EXPECT_ERROR(nn::ops::sdpa(fake({1, 4, 16, 64}, DType::F32), ka, ka, 0.125f), L3D_E_DTYPE, "bf16");
+  EXPECT_ERROR(nn::ops::sdpa(qa, fake({1, 2, 32, 64}, DType::BF16), fake({1, 2, 32, 64}, DType::BF16),
+                             0.125f),
+               L3D_E_SHAPE, "differ");
+  EXPECT_ERROR(nn::ops::sdpa(qa, ka, ka, 0.f), L3D_E_SHAPE, "positive");
+  EXPECT_ERROR((nn::Linear{fake({32, 64}, DType::F32), std::nullopt}.forward(fake({4, 64}, DType::BF16))),
+               L3D_E_DTYPE, "weight is bf16");
+  EXPECT_ERROR((nn::Linear{fake({32, 64}, DType::BF16), std::nullopt}.forward(fake({4, 48}, DType::BF16))),
+               L3D_E_SHAPE, "against weight");
+  EXPECT_ERROR(runtime::linear_small(fake({2, 64}, DType::BF16), fake({96, 32}, DType::BF16),
+                                     std::nullopt, std::nullopt, nn::Act::Silu, nn::Act::None),
+               L3D_E_SHAPE, "against w");
+  EXPECT_ERROR(runtime::patch_embed(fake({2, 3, 30, 28}, DType::BF16), fake({16, 3, 14, 14}, DType::BF16),
+                                    fake({16}, DType::BF16), fake({5, 16}, DType::BF16),
+                                    fake({16}, DType::BF16), std::nullopt, 14),
+               L3D_E_SHAPE, "whole patches");
+  EXPECT_ERROR(runtime::neighbor_pairs(fake({10, 3}, DType::I64)), L3D_E_SHAPE, "i32");
 }
 
 // Without a device: allocation fails with a CUDA error; and with a host
@@ -133,6 +155,12 @@ static void without_device() {
                L3D_E_SHAPE, "l3d_layer_norm_modulate: ");
   EXPECT_ERROR(runtime::gated_residual(x, x, fake({3, 64}, DType::BF16)), L3D_E_SHAPE,
                "l3d_gated_residual: ");
+  // the attention's own envelope (head dim 64 or 128) and the seam's gate batch
+  Tensor q96 = Tensor::from_device_ptr(kFake, Layout::contiguous({1, 2, 16, 96}), DType::BF16, d);
+  EXPECT_ERROR(nn::ops::sdpa(q96, q96, q96, 0.1f), L3D_E_UNSUPPORTED, "head dim must be 64 or 128");
+  EXPECT_ERROR(runtime::residual_layer_norm_modulate(x, x, fake({5, 64}, DType::BF16), std::nullopt,
+                                                     std::nullopt, std::nullopt, std::nullopt, 1e-5f),
+               L3D_E_SHAPE, "l3d_residual_layer_norm_modulate: ");
 }
 
 int main() {
